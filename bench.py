@@ -1,0 +1,425 @@
+"""Benchmark of the decode-time KV-cache hot path (one JSON line on rank 0).
+
+Workload (default): Qwen3-8B full-attention decode, 36 layers, 32 query heads,
+8 kv heads, head_dim 128, bf16, 8191 cached tokens + 1 appended per layer
+(S = 8192), paged layout (page 16, seeded shuffled block table per layer). One step
+= for every layer, one fused call: q head-RMSNorm + RoPE, k head-RMSNorm + RoPE +
+page write of the new token (append), split-KV attention over all 8192 positions.
+Synthetic seeded data; the step's inputs (1.2 GB of K/V) are larger than L2.
+
+metric: decode-attn KV-read GB/s = (K+V bytes read for S tokens + append bytes) per
+layer x layers / step time; also reported as us per layer. N > 1 GPUs run
+independent replicas (one process per GPU, no collective on this path).
+
+`--impl reference` (rank 0 only): the reference's algorithm on the host cores — the
+oracle's C restatement of src/kernels.cu's paged attention with OpenMP over heads —
+as the line's value, plus the reference's own kernels built for sm_100a timed on
+the GPU for the same layers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no samples
+            self.nvml = None
+
+    def _run(self):
+        n = self.nvml
+        names = {
+            0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+            0x80: "hw_power_brake_slowdown",
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for bit, name in names.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def layer_bytes(cfg) -> int:
+    return cfg.kv_read_bytes() + cfg.append_bytes()
+
+
+def build_step(inp, ws, stream_ptr=None):
+    """Returns a callable issuing one decode step (all layers) through the public API."""
+    import qwenincuda_b200 as q
+
+    cfg = inp.cfg
+    args = []
+    for layer in range(inp.q.shape[0]):
+        args.append(q.ops.decode_args(
+            q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=inp.out[layer],
+            num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
+            page_table=inp.page_table[layer] if inp.paged else None, page_size=cfg.page_size,
+            gate=None if inp.gate is None else inp.gate[layer], q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w,
+            k_new=inp.k_new[layer], v_new=inp.v_new[layer], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True,
+            fuse_append=True, workspace=ws, cache_tokens=inp.cache_tokens))
+    L = q.lib()
+    import ctypes
+
+    def step():
+        s = torch.cuda.current_stream().cuda_stream
+        for a in args:
+            rc = L.qic_decode_attention(ctypes.byref(a), s)
+            if rc != 0:
+                raise q.QicError(rc, "qic_decode_attention")
+
+    return step
+
+
+def capture(fn):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm the per-device attribute set-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, steps, warmup, world):
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end) / steps, world)
+
+
+def cpu_baseline(cfg, budget_s=6.0):
+    """The oracle (C restatement of the reference's paged attention, OpenMP) on a
+    bounded sample of the workload's layers on this host."""
+    from oracle.oracle import Oracle
+    from qwenincuda_b200.workloads import make_attention_inputs
+
+    orc = Oracle()
+    threads = orc.num_threads()
+    inp = make_attention_inputs(cfg, paged=True, layers=1, device="cpu")
+    H, Hkv, d, S = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len
+    kc = inp.k_cache[0].view(-1, Hkv * d)
+    vc = inp.v_cache[0].view(-1, Hkv * d)
+    layers = 0
+    t0 = time.perf_counter()
+    while True:
+        orc.attention(inp.q[0].flatten(), kc, vc, H, Hkv, d, S, page_table=inp.page_table[0], page_size=cfg.page_size)
+        layers += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    per_layer = el / layers
+    return {
+        "value": round(layer_bytes(cfg) / per_layer / 1e9, 3),
+        "unit": "GB/s",
+        "us_per_layer": round(per_layer * 1e6, 1),
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{layers} layers of paged attention at S={S} (H={H}, Hkv={Hkv}, d={d}) in {el:.1f} s",
+    }
+
+
+def reference_gpu(cfg, layers, steps, warmup):
+    """The reference's own kernels (src/kernels.cu built for sm_100a with
+    --use_fast_math) driving the same per-layer sequence as src/model.cpp:633-650."""
+    from oracle.oracle import RefKernels
+    from qwenincuda_b200.workloads import make_attention_inputs
+
+    dtype = torch.bfloat16
+    ref = RefKernels(dtype)
+    inp = make_attention_inputs(cfg, paged=True, layers=layers)
+    H, Hkv, d, S, P, pos = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len, cfg.page_size, cfg.position
+    lib = ref.lib
+    from oracle.oracle import _p
+
+    qbuf = torch.empty(H * d, device="cuda", dtype=dtype)
+    kbuf = torch.empty(Hkv * d, device="cuda", dtype=dtype)
+    slots = [int(inp.page_table[i][pos // P]) * P + pos % P for i in range(layers)]
+
+    def step():
+        for i in range(layers):
+            qbuf.copy_(inp.q[i].flatten())
+            kbuf.copy_(inp.k_new[i].flatten())
+            lib.qicref_head_rmsnorm(_p(qbuf), _p(inp.q_norm_w), H, d, cfg.eps, _p(qbuf))
+            lib.qicref_head_rmsnorm(_p(kbuf), _p(inp.k_norm_w), Hkv, d, cfg.eps, _p(kbuf))
+            lib.qicref_rope_inplace(_p(qbuf), H, d, pos, cfg.rope_theta)
+            lib.qicref_rope_inplace(_p(kbuf), Hkv, d, pos, cfg.rope_theta)
+            kc = inp.k_cache[i].view(-1, Hkv * d)
+            vc = inp.v_cache[i].view(-1, Hkv * d)
+            lib.qicref_copy_row(_p(kc), _p(kbuf), slots[i], Hkv * d)
+            lib.qicref_copy_row(_p(vc), _p(inp.v_new[i].flatten()), slots[i], Hkv * d)
+            lib.qicref_paged_attention(_p(qbuf), _p(kc), _p(vc), _p(inp.page_table[i]), P, H, Hkv, d, S,
+                                       _p(inp.out[i]))
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    per_layer_us = ms * 1000 / layers
+    return {
+        "value": round(layer_bytes(cfg) / (per_layer_us * 1e-6) / 1e9, 3),
+        "unit": "GB/s",
+        "us_per_layer": round(per_layer_us, 1),
+        "layers_timed": layers,
+        "build": "src/kernels.cu unmodified, nvcc -gencode arch=compute_100a,code=sm_100a --use_fast_math, bf16 instance",
+    }
+
+
+def run_reference_arm(args, world, rank):
+    from qwenincuda_b200.workloads import CONFIGS
+
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.workload]
+    cb = cpu_baseline(cfg, budget_s=max(2.0, min(20.0, 0.5 * args.steps)))
+    line = {
+        "impl": "reference",
+        "metric": "decode-attn KV-read GB/s",
+        "value": cb["value"],
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(cb["us_per_layer"] * cfg.layers / 1000, 3),
+        "us_per_layer": cb["us_per_layer"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "layout": "paged", "layers": cfg.layers, "seq_len": cfg.seq_len,
+                   "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    try:
+        line["reference_kernels_sm100a"] = reference_gpu(cfg, layers=min(4, cfg.layers), steps=max(1, args.steps // 10),
+                                                         warmup=1)
+    except Exception as exc:  # the GPU comparator is extra information only
+        line["reference_kernels_sm100a"] = {"unavailable": str(exc)[:200]}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="qwen3_8b_s8192")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+
+    import qwenincuda_b200 as q
+    from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
+
+    cfg = CONFIGS[args.workload]
+    peaks = load_peaks()
+    results = {}
+    for layout in ("paged", "contiguous"):
+        inp = make_attention_inputs(cfg, paged=(layout == "paged"))
+        ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
+        step = build_step(inp, ws)
+        g = capture(step)
+        sampler = ClockSampler(local)
+        with sampler:
+            ms = time_graph(g, args.steps, args.warmup, world)
+        status = ws.status()
+        if status != 0:
+            raise RuntimeError(f"device status {status} after timed steps ({layout})")
+        results[layout] = dict(ms=ms, clocks=sampler.summary(), inp=inp, ws=ws, graph=g)
+        if layout == "paged":
+            # e2e: pinned host inputs -> device, the same public-API step, outputs -> pinned host
+            hq = torch.empty_like(inp.q, device="cpu").pin_memory()
+            hk = torch.empty_like(inp.k_new, device="cpu").pin_memory()
+            hv = torch.empty_like(inp.v_new, device="cpu").pin_memory()
+            hq.copy_(inp.q)
+            hk.copy_(inp.k_new)
+            hv.copy_(inp.v_new)
+            ho = torch.empty_like(inp.out, device="cpu").pin_memory()
+
+            def e2e_step():
+                inp.q.copy_(hq, non_blocking=True)
+                inp.k_new.copy_(hk, non_blocking=True)
+                inp.v_new.copy_(hv, non_blocking=True)
+                step()
+                ho.copy_(inp.out, non_blocking=True)
+
+            ge = capture(e2e_step)
+            ms_e2e = time_graph(ge, args.steps, args.warmup, world)
+            results["e2e"] = dict(ms=ms_e2e, h2d=hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2,
+                                  d2h=ho.numel() * 2)
+            del ge
+        del g
+        torch.cuda.synchronize()
+
+    lb = layer_bytes(cfg)
+    step_bytes = lb * cfg.layers
+    paged = results["paged"]
+    value = world * step_bytes / (paged["ms"] * 1e-3) / 1e9
+    per_launch_ms = paged["ms"] / cfg.layers
+    achieved = lb / (per_launch_ms * 1e-3) / 1e9
+    contiguous = results["contiguous"]
+    line = {
+        "metric": "decode-attn KV-read GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(paged["ms"], 4),
+        "us_per_layer": round(per_launch_ms * 1000, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": args.workload, "layout": "paged", "page_size": cfg.page_size, "layers": cfg.layers,
+            "seq_len": cfg.seq_len, "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads,
+            "head_dim": cfg.head_dim, "parallelism": f"replicas{world}" if world > 1 else "single",
+            "step": "per layer: fused q norm+RoPE, k norm+RoPE+page append, split-KV attention (CUDA graph)",
+            "l2": "step inputs 1.2 GB > 126 MB L2",
+        },
+        "contiguous": {"value": round(world * step_bytes / (contiguous["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                       "us_per_layer": round(contiguous["ms"] / cfg.layers * 1000, 3)},
+        "e2e": {"value": round(world * step_bytes / (results["e2e"]["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": results["e2e"]["h2d"], "d2h_bytes_per_step": results["e2e"]["d2h"],
+                "ms_per_step": round(results["e2e"]["ms"], 4)},
+        "roofline": {
+            "bound": "hbm", "kernel": "decode_attn_kernel", "achieved": round(achieved, 1),
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "peak_source": peaks["source"], "frac_of_8tbs": round(achieved / 8000.0, 4),
+            "bytes_per_launch": lb, "traffic": None,
+        },
+        "gpu_launches": cfg.layers * args.steps,
+        "clocks": paged["clocks"],
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

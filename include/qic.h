@@ -1,0 +1,179 @@
+/*
+ * qic.h — C-ABI of the QweninCuda decode-time KV-cache hot path for B200 (sm_100a).
+ *
+ * Plain C types only: device pointers as void*, sizes as int32/int64, CUDA streams
+ * as an opaque pointer (binary-compatible with cudaStream_t / CUstream). Every entry
+ * point returns a qic_status (0 = success) and never allocates device memory;
+ * scratch space is passed in by the caller (see qic_decode_workspace_bytes).
+ *
+ * Element types: QIC_DTYPE_F16 (the reference's `half`) or QIC_DTYPE_BF16.
+ *
+ * Reference interfaces replaced (paths inside the QweninCuda project):
+ *   launch_head_rmsnorm        include/kernels.cuh:7-8,   src/kernels.cu:78-112,392-396
+ *   launch_rope_inplace        include/kernels.cuh:13,    src/kernels.cu:150-183,418-424
+ *   launch_sigmoid_mul_inplace include/kernels.cuh:12,    src/kernels.cu:138-148,412-416
+ *   launch_flash_attention     include/kernels.cuh:15-16, src/kernels.cu:200-290,432-438
+ *   launch_paged_attention     include/kernels.cuh:17-19, src/kernels.cu:292-374,440-447
+ *   K/V append (cudaMemcpy D2D at position*kv_dim)        src/model.cpp:31-33,639-641
+ *   full-attention block body (norm, RoPE, append, attn)  src/model.cpp:633-652
+ *   GatedDeltaNet host loop (conv, delta rule, gated norm) src/model.cpp:692-793
+ * The exact C++ signatures of include/kernels.cuh are provided as well, by
+ * include/qic_kernels_compat.h, on top of these entry points.
+ */
+#ifndef QIC_H_
+#define QIC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qic_stream_t; /* same type as cudaStream_t */
+
+typedef enum qic_status {
+  QIC_SUCCESS = 0,
+  QIC_ERROR_INVALID_VALUE = 1,   /* null pointer, non-positive size, H % Hkv != 0, position outside cache */
+  QIC_ERROR_NOT_SUPPORTED = 2,   /* head_dim / group size / page size outside the compiled set */
+  QIC_ERROR_MISALIGNED = 3,      /* a pointer or row stride breaks the 16-byte TMA rule */
+  QIC_ERROR_WORKSPACE = 4,       /* workspace missing or smaller than required */
+  QIC_ERROR_CUDA = 5,            /* CUDA runtime or launch error (qic_last_cuda_error) */
+  QIC_ERROR_DEVICE_TIMEOUT = 6,  /* a bounded device-side wait gave up (device status word) */
+  QIC_ERROR_BAD_PAGE = 7,        /* a page-table entry points outside the cache (device status word) */
+  QIC_ERROR_PEER = 8             /* peer-exchange set-up failed */
+} qic_status;
+
+enum { QIC_DTYPE_F16 = 0, QIC_DTYPE_BF16 = 1 };
+
+/* Bits of the device status word kept in the workspace (qic_workspace_status). */
+enum {
+  QIC_DEV_TIMEOUT = 1,           /* a bounded wait timed out */
+  QIC_DEV_BAD_PAGE = 2,          /* an out-of-range page-table entry was clamped to page 0 */
+  QIC_DEV_PEER_TIMEOUT = 4       /* a peer never published its partial */
+};
+
+/* Flags of qic_decode_args.flags */
+enum {
+  QIC_FUSE_Q_PROLOGUE = 1,       /* q := RoPE(head_rmsnorm(q, q_norm_w)) inside the attention kernel */
+  QIC_FUSE_APPEND = 2            /* k_new/v_new appended at position seq_len-1 inside the kernel */
+};
+
+const char* qic_status_string(int status);
+int qic_last_cuda_error(void);    /* cudaError_t of the last QIC_ERROR_CUDA on this thread */
+int qic_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Standalone ops, numerically identical to the reference kernels.           */
+/* ------------------------------------------------------------------------- */
+
+/* out[h,:] = x[h,:] * rsqrt(mean(x[h,:]^2) + eps) * weight, rounded to dtype.
+ * Replaces launch_head_rmsnorm (include/kernels.cuh:7-8). x == out allowed. */
+int qic_head_rmsnorm(int dtype, const void* x, const void* weight, int num_heads, int head_dim, float eps,
+                     void* out, qic_stream_t stream);
+
+/* Rotate-half RoPE over all head_dim dims, in place.
+ * Replaces launch_rope_inplace (include/kernels.cuh:13). */
+int qic_rope_inplace(int dtype, void* x, int num_heads, int head_dim, int position, float rope_theta,
+                     qic_stream_t stream);
+
+/* x[i] *= sigmoid(gate[i]). Replaces launch_sigmoid_mul_inplace (include/kernels.cuh:12). */
+int qic_sigmoid_mul_inplace(int dtype, void* x, const void* gate, int n, qic_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* K/V append fused with k head-RMSNorm and RoPE.                            */
+/* ------------------------------------------------------------------------- */
+
+/* k_cache[slot] = RoPE(head_rmsnorm(k_new, k_norm_w)), v_cache[slot] = v_new, for all
+ * num_kv_heads heads, where slot = page_table[position/page_size]*page_size +
+ * position%page_size (paged) or slot = position (page_table == NULL). Byte-identical
+ * to the reference chain launch_head_rmsnorm -> launch_rope_inplace -> cudaMemcpy
+ * (src/model.cpp:634,637,639-641), written straight into the page that
+ * launch_paged_attention reads for token `position` (src/kernels.cu:320-323).
+ * Caches are [cache_tokens, num_kv_heads, head_dim]. */
+int qic_kv_append(int dtype, const void* k_new, const void* v_new, const void* k_norm_w, float eps,
+                  float rope_theta, int position, void* k_cache, void* v_cache, const int32_t* page_table,
+                  int page_size, int64_t cache_tokens, int num_kv_heads, int head_dim, qic_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Split-KV decode attention (contiguous = flash layout, or paged).          */
+/* ------------------------------------------------------------------------- */
+
+typedef struct qic_decode_args {
+  int32_t dtype;            /* QIC_DTYPE_* */
+  int32_t num_heads;        /* H query heads */
+  int32_t num_kv_heads;     /* Hkv, H % Hkv == 0, group H/Hkv <= 8 */
+  int32_t head_dim;         /* d in {64, 128, 256} */
+  int32_t seq_len;          /* S tokens attended (position+1 when appending); 0 writes zeros */
+  int32_t page_size;        /* tokens per page when page_table != NULL (multiple of 8) */
+  int64_t cache_tokens;     /* token rows in k_cache / v_cache (bounds for loads and table entries) */
+  const void* q;            /* [H, d] (raw projection when QIC_FUSE_Q_PROLOGUE) */
+  void* k_cache;            /* [cache_tokens, Hkv, d], 16-byte aligned */
+  void* v_cache;            /* [cache_tokens, Hkv, d], 16-byte aligned */
+  const int32_t* page_table;/* [ceil(S/page_size)] physical page of each logical page; NULL = contiguous */
+  const void* gate;         /* [H, d] output gate (out *= sigmoid(gate)) or NULL */
+  void* out;                /* [H, d] */
+  uint32_t flags;           /* QIC_FUSE_* */
+  float eps;                /* head-RMSNorm epsilon (fused prologue / append) */
+  float rope_theta;         /* RoPE base (fused prologue / append) */
+  const void* q_norm_w;     /* [d] (QIC_FUSE_Q_PROLOGUE) */
+  const void* k_norm_w;     /* [d] (QIC_FUSE_APPEND) */
+  const void* k_new;        /* [Hkv, d] raw k projection (QIC_FUSE_APPEND) */
+  const void* v_new;        /* [Hkv, d] v projection (QIC_FUSE_APPEND) */
+  void* workspace;          /* scratch from the caller, zeroed once by qic_workspace_init */
+  size_t workspace_bytes;
+  int32_t num_splits;       /* KV splits per kv head; 0 = chosen from the SM count */
+  int32_t reserved;
+} qic_decode_args;
+
+/* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len). */
+size_t qic_decode_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int max_seq_len);
+
+/* Zeroes a workspace (counters and the device status word). Call once after allocating it. */
+int qic_workspace_init(void* workspace, size_t bytes, qic_stream_t stream);
+
+/* Reads and clears the device status word (QIC_DEV_* bits); synchronises `stream`. */
+int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status);
+
+/* context[h,:] = sum_t softmax_t(q_h . K[t,h/g] / sqrt(d)) V[t,h/g] over t < seq_len,
+ * optionally preceded by the fused q prologue and append and followed by the gate.
+ * Replaces launch_flash_attention / launch_paged_attention (include/kernels.cuh:15-19)
+ * and, with flags, the block src/model.cpp:633-652. */
+int qic_decode_attention(const qic_decode_args* args, qic_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Qwen3.5 GatedDeltaNet decode step (state resident on the device).          */
+/* ------------------------------------------------------------------------- */
+
+typedef struct qic_gdn_args {
+  int32_t dtype;            /* element type of the 16-bit inputs and of out */
+  int32_t num_k_heads;      /* Hk */
+  int32_t num_v_heads;      /* Hv, Hv % Hk == 0, Hv/Hk in {1, 2, 4} */
+  int32_t k_head_dim;       /* dk == 128 */
+  int32_t v_head_dim;       /* dv == 128 */
+  int32_t conv_kernel;      /* K in [1, 8] */
+  float eps;                /* gated RMSNorm epsilon */
+  int32_t reserved;
+  const void* qkv;          /* [2*Hk*dk + Hv*dv] in_proj_qkv output (conv input) */
+  const void* z;            /* [Hv*dv] */
+  const void* b;            /* [Hv] */
+  const void* a;            /* [Hv] */
+  const void* conv_w;       /* [conv_dim, K] */
+  const void* dt_bias;      /* [Hv] */
+  const void* a_log;        /* [Hv] */
+  const void* norm_w;       /* [dv] */
+  float* conv_state;        /* [conv_dim, K] fp32, updated in place */
+  float* recurrent_state;   /* [Hv, dk, dv] fp32, updated in place */
+  void* out;                /* [Hv*dv] gated-norm output (input of out_proj) */
+} qic_gdn_args;
+
+/* One decode step of src/model.cpp:692-791 on the device: conv-state shift and causal
+ * conv + SiLU, L2-norm of q/k, head repeat, beta/g gates, delta-rule state update and
+ * read-out, gated RMSNorm. */
+int qic_gated_delta_decode(const qic_gdn_args* args, qic_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QIC_H_ */

@@ -1,0 +1,148 @@
+"""ctypes declarations of include/qic.h (the C-ABI of libqic.so)."""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+QIC_DTYPE_F16 = 0
+QIC_DTYPE_BF16 = 1
+QIC_FUSE_Q_PROLOGUE = 1
+QIC_FUSE_APPEND = 2
+
+QIC_DEV_TIMEOUT = 1
+QIC_DEV_BAD_PAGE = 2
+QIC_DEV_PEER_TIMEOUT = 4
+
+STATUS_NAMES = {
+    0: "QIC_SUCCESS",
+    1: "QIC_ERROR_INVALID_VALUE",
+    2: "QIC_ERROR_NOT_SUPPORTED",
+    3: "QIC_ERROR_MISALIGNED",
+    4: "QIC_ERROR_WORKSPACE",
+    5: "QIC_ERROR_CUDA",
+    6: "QIC_ERROR_DEVICE_TIMEOUT",
+    7: "QIC_ERROR_BAD_PAGE",
+    8: "QIC_ERROR_PEER",
+}
+
+_PKG = Path(__file__).resolve().parent
+
+
+def lib_path() -> Path:
+    return _PKG / "libqic.so"
+
+
+class QicError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        name = STATUS_NAMES.get(status, str(status))
+        msg = f"{what}: {name}" if what else name
+        if status == 5 and _LIB is not None:
+            msg += f" (cudaError {_LIB.qic_last_cuda_error()})"
+        super().__init__(msg)
+
+
+class DecodeArgs(ctypes.Structure):
+    """Mirror of qic_decode_args."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("cache_tokens", ctypes.c_int64),
+        ("q", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("page_table", ctypes.c_void_p),
+        ("gate", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("flags", ctypes.c_uint32),
+        ("eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+        ("q_norm_w", ctypes.c_void_p),
+        ("k_norm_w", ctypes.c_void_p),
+        ("k_new", ctypes.c_void_p),
+        ("v_new", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("num_splits", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class GdnArgs(ctypes.Structure):
+    """Mirror of qic_gdn_args."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("num_k_heads", ctypes.c_int32),
+        ("num_v_heads", ctypes.c_int32),
+        ("k_head_dim", ctypes.c_int32),
+        ("v_head_dim", ctypes.c_int32),
+        ("conv_kernel", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
+        ("qkv", ctypes.c_void_p),
+        ("z", ctypes.c_void_p),
+        ("b", ctypes.c_void_p),
+        ("a", ctypes.c_void_p),
+        ("conv_w", ctypes.c_void_p),
+        ("dt_bias", ctypes.c_void_p),
+        ("a_log", ctypes.c_void_p),
+        ("norm_w", ctypes.c_void_p),
+        ("conv_state", ctypes.c_void_p),
+        ("recurrent_state", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+    ]
+
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); every function declared in include/qic.h
+SIGNATURES = {
+    "qic_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "qic_last_cuda_error": (ctypes.c_int, []),
+    "qic_version": (ctypes.c_int, []),
+    "qic_head_rmsnorm": (ctypes.c_int, [ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int, _f32, _vp, _vp]),
+    "qic_rope_inplace": (ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32, _vp]),
+    "qic_sigmoid_mul_inplace": (ctypes.c_int, [ctypes.c_int, _vp, _vp, ctypes.c_int, _vp]),
+    "qic_kv_append": (
+        ctypes.c_int,
+        [ctypes.c_int, _vp, _vp, _vp, _f32, _f32, ctypes.c_int, _vp, _vp, _vp, ctypes.c_int, _i64, ctypes.c_int,
+         ctypes.c_int, _vp],
+    ),
+    "qic_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qic_workspace_init": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp]),
+    "qic_workspace_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int)]),
+    "qic_decode_attention": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
+    "qic_gated_delta_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), _vp]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libqic.so once. Raises if it has not been built: there is no fallback."""
+    global _LIB
+    if _LIB is None:
+        path = lib_path()
+        if not path.exists():
+            raise ImportError(f"{path} is missing; build it with `python -m qwenincuda_b200.build`")
+        handle = ctypes.CDLL(str(path), mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = handle
+    return _LIB
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise QicError(status, what)

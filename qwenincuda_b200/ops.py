@@ -1,0 +1,167 @@
+"""Tensor-level wrappers over the C-ABI, mirroring the reference's call surface.
+
+Names and argument order follow include/kernels.cuh of the QweninCuda project
+(launch_head_rmsnorm, launch_rope_inplace, launch_sigmoid_mul_inplace,
+launch_flash_attention, launch_paged_attention) with torch tensors in place of raw
+device pointers, plus the fused entry points this library adds (kv_append,
+decode_attention, gated_delta_decode). Every call runs on the current torch CUDA
+stream unless a stream is given, and raises QicError on a non-success status.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .abi import (
+    QIC_DTYPE_BF16,
+    QIC_DTYPE_F16,
+    QIC_FUSE_APPEND,
+    QIC_FUSE_Q_PROLOGUE,
+    DecodeArgs,
+    GdnArgs,
+    check,
+    lib,
+)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return QIC_DTYPE_BF16
+    if t.dtype == torch.float16:
+        return QIC_DTYPE_F16
+    raise TypeError(f"unsupported dtype {t.dtype}; expected bfloat16 or float16")
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor")
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+class Workspace:
+    """Caller-owned split-KV scratch (partials, merge counters, device status word)."""
+
+    def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, max_seq_len: int, device=None,
+                 stream=None):
+        nbytes = lib().qic_decode_workspace_bytes(num_heads, num_kv_heads, head_dim, max_seq_len)
+        if nbytes == 0:
+            raise ValueError("invalid workspace shape")
+        self.nbytes = int(nbytes)
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+        check(lib().qic_workspace_init(self.buf.data_ptr(), self.nbytes, _stream(stream)), "qic_workspace_init")
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def status(self, stream=None) -> int:
+        """Reads and clears the device status word (QIC_DEV_* bits)."""
+        v = ctypes.c_int(0)
+        check(lib().qic_workspace_status(self.ptr, _stream(stream), ctypes.byref(v)), "qic_workspace_status")
+        return v.value
+
+
+def launch_head_rmsnorm(x, weight, num_heads, head_dim, eps, out, stream=None):
+    check(lib().qic_head_rmsnorm(dtype_code(x), _ptr(x), _ptr(weight), num_heads, head_dim, eps, _ptr(out),
+                                 _stream(stream)), "launch_head_rmsnorm")
+
+
+def launch_rope_inplace(q_or_k, num_heads, head_dim, position, rope_theta, stream=None):
+    check(lib().qic_rope_inplace(dtype_code(q_or_k), _ptr(q_or_k), num_heads, head_dim, position, rope_theta,
+                                 _stream(stream)), "launch_rope_inplace")
+
+
+def launch_sigmoid_mul_inplace(x, gate, n, stream=None):
+    check(lib().qic_sigmoid_mul_inplace(dtype_code(x), _ptr(x), _ptr(gate), n, _stream(stream)),
+          "launch_sigmoid_mul_inplace")
+
+
+def kv_append(k_new, v_new, k_norm_w, eps, rope_theta, position, k_cache, v_cache, num_kv_heads, head_dim,
+              page_table=None, page_size=16, cache_tokens=None, stream=None):
+    """Fused head-RMSNorm(k) + RoPE(k) + write of k and v into the slot of `position`."""
+    if cache_tokens is None:
+        cache_tokens = k_cache.numel() // (num_kv_heads * head_dim)
+    check(lib().qic_kv_append(dtype_code(k_cache), _ptr(k_new), _ptr(v_new), _ptr(k_norm_w), eps, rope_theta,
+                              position, _ptr(k_cache), _ptr(v_cache), _ptr(page_table), page_size, cache_tokens,
+                              num_kv_heads, head_dim, _stream(stream)), "kv_append")
+
+
+def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, seq_len, page_table=None,
+                page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
+                rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
+                cache_tokens=None) -> DecodeArgs:
+    a = DecodeArgs()
+    a.dtype = dtype_code(k_cache)
+    a.num_heads = num_heads
+    a.num_kv_heads = num_kv_heads
+    a.head_dim = head_dim
+    a.seq_len = seq_len
+    a.page_size = page_size if page_table is not None else 0
+    a.cache_tokens = cache_tokens if cache_tokens is not None else k_cache.numel() // (num_kv_heads * head_dim)
+    a.q = _ptr(q)
+    a.k_cache = _ptr(k_cache)
+    a.v_cache = _ptr(v_cache)
+    a.page_table = _ptr(page_table)
+    a.gate = _ptr(gate)
+    a.out = _ptr(out)
+    a.flags = (QIC_FUSE_Q_PROLOGUE if fuse_q else 0) | (QIC_FUSE_APPEND if fuse_append else 0)
+    a.eps = eps
+    a.rope_theta = rope_theta
+    a.q_norm_w = _ptr(q_norm_w)
+    a.k_norm_w = _ptr(k_norm_w)
+    a.k_new = _ptr(k_new)
+    a.v_new = _ptr(v_new)
+    if workspace is not None:
+        a.workspace = workspace.ptr
+        a.workspace_bytes = workspace.nbytes
+    a.num_splits = num_splits
+    return a
+
+
+def decode_attention(stream=None, **kw):
+    """Split-KV decode attention; see qic_decode_attention in include/qic.h."""
+    a = decode_args(**kw)
+    check(lib().qic_decode_attention(ctypes.byref(a), _stream(stream)), "qic_decode_attention")
+
+
+def launch_flash_attention(q, k_cache, v_cache, num_heads, num_kv_heads, head_dim, seq_len, context,
+                           workspace=None, stream=None):
+    decode_attention(q=q, k_cache=k_cache, v_cache=v_cache, out=context, num_heads=num_heads,
+                     num_kv_heads=num_kv_heads, head_dim=head_dim, seq_len=seq_len, workspace=workspace,
+                     stream=stream)
+
+
+def launch_paged_attention(q, k_cache, v_cache, page_table, page_size, num_heads, num_kv_heads, head_dim, seq_len,
+                           context, workspace=None, stream=None):
+    decode_attention(q=q, k_cache=k_cache, v_cache=v_cache, out=context, num_heads=num_heads,
+                     num_kv_heads=num_kv_heads, head_dim=head_dim, seq_len=seq_len, page_table=page_table,
+                     page_size=page_size, workspace=workspace, stream=stream)
+
+
+def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, out,
+                       num_k_heads, num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6,
+                       stream=None):
+    """One GatedDeltaNet decode step; conv_state and recurrent_state (fp32) are updated in place."""
+    g = GdnArgs()
+    g.dtype = dtype_code(qkv)
+    g.num_k_heads = num_k_heads
+    g.num_v_heads = num_v_heads
+    g.k_head_dim = k_head_dim
+    g.v_head_dim = v_head_dim
+    g.conv_kernel = conv_kernel
+    g.eps = eps
+    g.qkv, g.z, g.b, g.a = _ptr(qkv), _ptr(z), _ptr(b), _ptr(a)
+    g.conv_w, g.dt_bias, g.a_log, g.norm_w = _ptr(conv_w), _ptr(dt_bias), _ptr(a_log), _ptr(norm_w)
+    g.conv_state, g.recurrent_state, g.out = _ptr(conv_state), _ptr(recurrent_state), _ptr(out)
+    check(lib().qic_gated_delta_decode(ctypes.byref(g), _stream(stream)), "qic_gated_delta_decode")

@@ -1,0 +1,114 @@
+"""GPU: the append path (head RMSNorm + RoPE of k, page write, v copy) and the
+standalone norm / RoPE / gate ops are byte-identical to the reference's own kernels
+(src/kernels.cu compiled unchanged for sm_100a with --use_fast_math, oracle/_ref)."""
+import pytest
+import torch
+
+import qwenincuda_b200 as q
+from oracle.oracle import RefKernels
+
+pytestmark = pytest.mark.gpu
+DTYPES = [torch.bfloat16, torch.float16]
+
+
+def _gen(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def _mismatch(a, b):
+    return int((a.view(torch.int16) != b.view(torch.int16)).sum().item())
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("d", [64, 128, 256])
+def test_head_rmsnorm_bitexact(dtype, d):
+    ref = RefKernels(dtype)
+    g = _gen(d)
+    H = 256
+    x = (torch.randn(H * d, generator=g, device="cuda") * 2).to(dtype)
+    w = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(dtype)
+    want = torch.empty_like(x)
+    ref.head_rmsnorm(x, w, H, d, 1e-6, want)
+    got = torch.empty_like(x)
+    q.launch_head_rmsnorm(x, w, H, d, 1e-6, got)
+    torch.cuda.synchronize()
+    assert _mismatch(got, want) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("pos", [0, 1, 7, 1024, 8191, 32768, 131072])
+def test_rope_bitexact(dtype, pos):
+    ref = RefKernels(dtype)
+    g = _gen(pos + 1)
+    H, d = 32, 128
+    x = torch.randn(H * d, generator=g, device="cuda").to(dtype)
+    want = x.clone()
+    ref.rope_inplace(want, H, d, pos, 1.0e6)
+    got = x.clone()
+    q.launch_rope_inplace(got, H, d, pos, 1.0e6)
+    torch.cuda.synchronize()
+    assert _mismatch(got, want) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_sigmoid_mul_bitexact(dtype):
+    ref = RefKernels(dtype)
+    g = _gen(11)
+    n = 16 * 256
+    x = torch.randn(n, generator=g, device="cuda").to(dtype)
+    gate = torch.randn(n, generator=g, device="cuda").to(dtype)
+    want = x.clone()
+    ref.sigmoid_mul_inplace(want, gate, n)
+    got = x.clone()
+    q.launch_sigmoid_mul_inplace(got, gate, n)
+    torch.cuda.synchronize()
+    assert _mismatch(got, want) == 0
+
+
+def _append_case(dtype, Hkv, d, pos, P, seed):
+    g = _gen(seed)
+    npages = pos // P + 1
+    tokens = npages * P
+    kc = (torch.randn(tokens, Hkv * d, generator=g, device="cuda") * 0.5).to(dtype)
+    vc = (torch.randn(tokens, Hkv * d, generator=g, device="cuda") * 0.5).to(dtype)
+    k_new = torch.randn(Hkv * d, generator=g, device="cuda").to(dtype)
+    v_new = torch.randn(Hkv * d, generator=g, device="cuda").to(dtype)
+    w = (1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(dtype)
+    table = torch.randperm(npages, generator=g, device="cuda").to(torch.int32)
+    return kc, vc, k_new, v_new, w, table
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("Hkv,d,pos,P", [(8, 128, 1024, 16), (4, 256, 32768, 16), (8, 64, 77, 32),
+                                         (8, 128, 131072, 16)])
+@pytest.mark.parametrize("paged", [True, False])
+def test_kv_append_bitexact(dtype, Hkv, d, pos, P, paged):
+    ref = RefKernels(dtype)
+    kc, vc, k_new, v_new, w, table = _append_case(dtype, Hkv, d, pos, P, seed=pos + d)
+    slot = int(table[pos // P]) * P + pos % P if paged else pos
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    ref.append_chain(k_new, v_new, w, 1e-6, 1.0e6, pos, kc_ref, vc_ref, Hkv, d, slot)
+    q.kv_append(k_new, v_new, w, 1e-6, 1.0e6, pos, kc, vc, Hkv, d, page_table=table if paged else None,
+                page_size=P)
+    torch.cuda.synchronize()
+    assert _mismatch(vc, vc_ref) == 0
+    assert _mismatch(kc, kc_ref) == 0
+    # only the slot row changed
+    assert _mismatch(kc[slot], kc_ref[slot]) == 0
+
+
+def test_reference_head_rmsnorm_is_repeatable():
+    """The reference sums squares with a shared-memory atomicAdd; record whether its
+    bytes repeat run to run on this GPU (the bit-exact claims above rely on it)."""
+    dtype = torch.float16
+    ref = RefKernels(dtype)
+    g = _gen(5)
+    H, d = 512, 128
+    x = torch.randn(H * d, generator=g, device="cuda").to(dtype)
+    w = torch.ones(d, device="cuda", dtype=dtype)
+    first = torch.empty_like(x)
+    ref.head_rmsnorm(x, w, H, d, 1e-6, first)
+    for _ in range(10):
+        again = torch.empty_like(x)
+        ref.head_rmsnorm(x, w, H, d, 1e-6, again)
+        assert _mismatch(again, first) == 0

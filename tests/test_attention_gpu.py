@@ -1,0 +1,207 @@
+"""GPU: split-KV decode attention (contiguous and paged) against the reference's own
+flash/paged kernels (oracle/_ref) and the CPU oracle, within max-abs 2e-3 / rel 1e-2,
+over the benchmark shapes and the edge cases (short, ragged and empty sequences,
+page sizes, split counts, GQA groups, head dims, bad page entries)."""
+import pytest
+import torch
+
+import qwenincuda_b200 as q
+from conftest import allclose_report
+from oracle.oracle import RefKernels
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _gen(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def _inputs(H, Hkv, d, S, P, dtype, seed, extra_pages=0):
+    g = _gen(seed)
+    npages = max(1, (S + P - 1) // P) + extra_pages
+    tokens = npages * P
+    qv = torch.randn(H * d, generator=g, device="cuda").to(dtype)
+    kc = (torch.randn(tokens, Hkv * d, generator=g, device="cuda") * 0.5).to(dtype)
+    vc = (torch.randn(tokens, Hkv * d, generator=g, device="cuda") * 0.5).to(dtype)
+    table = torch.randperm(npages, generator=g, device="cuda").to(torch.int32)
+    return qv, kc, vc, table
+
+
+def _ours(qv, kc, vc, H, Hkv, d, S, table=None, P=16, splits=0, ws=True, gate=None):
+    out = torch.full((H * d,), float("nan"), device="cuda", dtype=qv.dtype)
+    w = q.Workspace(H, Hkv, d, max(S, 1)) if ws else None
+    q.decode_attention(q=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=S,
+                       page_table=table, page_size=P, gate=gate, workspace=w, num_splits=splits)
+    torch.cuda.synchronize()
+    if w is not None:
+        assert w.status() == 0
+    return out
+
+
+def _ref(qv, kc, vc, H, Hkv, d, S, table=None, P=16):
+    ref = RefKernels(qv.dtype)
+    out = torch.empty(H * d, device="cuda", dtype=qv.dtype)
+    if table is None:
+        ref.flash_attention(qv, kc, vc, H, Hkv, d, S, out)
+    else:
+        ref.paged_attention(qv, kc, vc, table, P, H, Hkv, d, S, out)
+    return out
+
+
+CASES = [
+    # H, Hkv, d, S, P
+    (16, 8, 128, 1025, 16),     # Qwen3-0.6B shape, S = 1024 cached + 1
+    (32, 8, 128, 8192, 16),     # Qwen3-8B shape
+    (16, 4, 256, 4097, 16),     # Qwen3.5 gated-attention shape (shorter S)
+    (8, 8, 64, 100, 8),
+    (64, 8, 128, 777, 32),      # group 8
+    (8, 8, 128, 1, 16),
+    (8, 8, 128, 2, 16),
+    (16, 8, 128, 31, 16),
+    (16, 8, 128, 32, 16),
+    (16, 8, 128, 33, 16),
+    (16, 8, 128, 129, 48),      # page size not a power of two (box height 16)
+    (16, 8, 128, 300, 64),      # pages larger than a stage
+    (4, 2, 256, 95, 24),        # box height 8
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,Hkv,d,S,P", CASES)
+@pytest.mark.parametrize("paged", [True, False])
+def test_attention_vs_reference(dtype, H, Hkv, d, S, P, paged):
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, dtype, seed=S * 3 + d + H)
+    tbl = table if paged else None
+    want = _ref(qv, kc, vc, H, Hkv, d, S, tbl, P)
+    got = _ours(qv, kc, vc, H, Hkv, d, S, tbl, P)
+    ok, err, idx = allclose_report(got, want, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
+
+
+@pytest.mark.parametrize("S", [1025, 5000])
+def test_attention_vs_cpu_oracle(oracle, S):
+    H, Hkv, d, P = 32, 8, 128, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=S)
+    got = _ours(qv, kc, vc, H, Hkv, d, S, table, P)
+    want = oracle.attention(qv, kc, vc, H, Hkv, d, S, page_table=table, page_size=P)
+    ok, err, idx = allclose_report(got, want, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 64, 0])
+def test_split_counts_agree(splits):
+    H, Hkv, d, S, P = 32, 8, 128, 2049, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=17)
+    want = _ref(qv, kc, vc, H, Hkv, d, S, table, P)
+    got = _ours(qv, kc, vc, H, Hkv, d, S, table, P, splits=splits)
+    ok, err, _ = allclose_report(got, want, ATOL, RTOL)
+    assert ok, err
+
+
+def test_no_workspace_runs_one_split():
+    H, Hkv, d, S, P = 16, 8, 128, 600, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=23)
+    want = _ref(qv, kc, vc, H, Hkv, d, S, table, P)
+    got = _ours(qv, kc, vc, H, Hkv, d, S, table, P, ws=False)
+    ok, err, _ = allclose_report(got, want, ATOL, RTOL)
+    assert ok, err
+
+
+def test_empty_sequence_writes_zeros():
+    H, Hkv, d = 16, 8, 128
+    qv, kc, vc, _ = _inputs(H, Hkv, d, 16, 16, torch.bfloat16, seed=1)
+    got = _ours(qv, kc, vc, H, Hkv, d, 0)
+    assert torch.count_nonzero(got) == 0
+
+
+def test_gate_epilogue():
+    H, Hkv, d, S, P = 16, 4, 256, 3000, 16
+    dtype = torch.bfloat16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, dtype, seed=31)
+    gate = torch.randn(H * d, generator=_gen(32), device="cuda").to(dtype)
+    ref = RefKernels(dtype)
+    want = _ref(qv, kc, vc, H, Hkv, d, S, table, P)
+    ref.sigmoid_mul_inplace(want, gate, H * d)
+    got = _ours(qv, kc, vc, H, Hkv, d, S, table, P, gate=gate)
+    ok, err, _ = allclose_report(got, want, ATOL, RTOL)
+    assert ok, err
+
+
+def test_workspace_too_small_is_rejected():
+    H, Hkv, d, S = 32, 8, 128, 4096
+    qv, kc, vc, _ = _inputs(H, Hkv, d, S, 16, torch.bfloat16, seed=2)
+    small = q.Workspace(H, Hkv, d, 64)
+    out = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(q.QicError) as e:
+        q.decode_attention(q=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d,
+                           seq_len=S, workspace=small, num_splits=16)
+    assert e.value.status == 4
+
+
+def test_bad_page_entry_is_reported_not_faulted():
+    """An out-of-range page-table entry is caught by the kernel's bounds check,
+    clamped to page 0 and reported in the device status word."""
+    H, Hkv, d, S, P = 16, 8, 128, 256, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=3)
+    table = table.clone()
+    table[3] = 10 ** 6
+    out = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+    w = q.Workspace(H, Hkv, d, S)
+    q.decode_attention(q=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=S,
+                       page_table=table, page_size=P, workspace=w)
+    torch.cuda.synchronize()
+    assert w.status() & q.abi.QIC_DEV_BAD_PAGE
+    assert w.status() == 0  # cleared by the read
+
+
+def _reference_step(ref, inp, layer, paged):
+    """The reference full-attention block body src/model.cpp:633-652 (without the
+    projections): head-norm q and k, RoPE q and k, append, attention, gate."""
+    cfg = inp.cfg
+    H, Hkv, d, pos, P = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.position, cfg.page_size
+    qv = inp.q[layer].flatten().clone()
+    ref.head_rmsnorm(qv, inp.q_norm_w, H, d, cfg.eps, qv)
+    ref.rope_inplace(qv, H, d, pos, cfg.rope_theta)
+    kc = inp.k_cache[layer].view(-1, Hkv * d)
+    vc = inp.v_cache[layer].view(-1, Hkv * d)
+    table = inp.page_table[layer] if paged else None
+    slot = int(table[pos // P]) * P + pos % P if paged else pos
+    ref.append_chain(inp.k_new[layer].flatten(), inp.v_new[layer].flatten(), inp.k_norm_w, cfg.eps, cfg.rope_theta,
+                     pos, kc, vc, Hkv, d, slot)
+    out = torch.empty(H * d, device="cuda", dtype=qv.dtype)
+    if paged:
+        ref.paged_attention(qv, kc, vc, table, P, H, Hkv, d, cfg.seq_len, out)
+    else:
+        ref.flash_attention(qv, kc, vc, H, Hkv, d, cfg.seq_len, out)
+    if inp.gate is not None:
+        ref.sigmoid_mul_inplace(out, inp.gate[layer].flatten(), H * d)
+    return out
+
+
+@pytest.mark.parametrize("name", ["qwen3_0p6b_s1025", "qwen35_gated_s32769"])
+@pytest.mark.parametrize("paged", [True, False])
+def test_fused_decode_step_matches_reference_chain(name, paged):
+    from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
+
+    cfg = CONFIGS[name]
+    dtype = torch.bfloat16
+    mine = make_attention_inputs(cfg, paged=paged, layers=1, dtype=dtype)
+    theirs = make_attention_inputs(cfg, paged=paged, layers=1, dtype=dtype)
+    ref = RefKernels(dtype)
+    want = _reference_step(ref, theirs, 0, paged)
+    w = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
+    out = mine.out[0].flatten()
+    q.decode_attention(q=mine.q[0], k_cache=mine.k_cache[0], v_cache=mine.v_cache[0], out=out,
+                       num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                       seq_len=cfg.seq_len, page_table=mine.page_table[0] if paged else None,
+                       page_size=cfg.page_size, gate=None if mine.gate is None else mine.gate[0],
+                       q_norm_w=mine.q_norm_w, k_norm_w=mine.k_norm_w, k_new=mine.k_new[0], v_new=mine.v_new[0],
+                       eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True, fuse_append=True, workspace=w)
+    torch.cuda.synchronize()
+    assert w.status() == 0
+    # appended cache contents: byte-identical, whole cache
+    assert torch.equal(mine.k_cache.view(torch.int16), theirs.k_cache.view(torch.int16))
+    assert torch.equal(mine.v_cache.view(torch.int16), theirs.v_cache.view(torch.int16))
+    ok, err, idx = allclose_report(out, want, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
