@@ -50,13 +50,19 @@ enum { QIC_DTYPE_F16 = 0, QIC_DTYPE_BF16 = 1 };
 enum {
   QIC_DEV_TIMEOUT = 1,           /* a bounded wait timed out */
   QIC_DEV_BAD_PAGE = 2,          /* an out-of-range page-table entry was clamped to page 0 */
-  QIC_DEV_PEER_TIMEOUT = 4       /* a peer never published its partial */
+  QIC_DEV_PEER_TIMEOUT = 4,      /* a peer never published its partial */
+  QIC_DEV_BAD_PLAN = 8           /* a batched work item does not fit the workspace; it was skipped */
 };
 
 /* Flags of qic_decode_args.flags */
 enum {
   QIC_FUSE_Q_PROLOGUE = 1,       /* q := RoPE(head_rmsnorm(q, q_norm_w)) inside the attention kernel */
-  QIC_FUSE_APPEND = 2            /* k_new/v_new appended at position seq_len-1 inside the kernel */
+  QIC_FUSE_APPEND = 2,           /* k_new/v_new appended at position seq_len-1 inside the kernel */
+  QIC_PDL = 4                    /* programmatic dependent launch: the kernel may start while the previous
+                                    kernel in the stream runs and prefetch cached K/V rows (all but the
+                                    appended one) and page-table entries; q, k_new, v_new, gate and the
+                                    workspace are touched only after that kernel has completed. The
+                                    previous kernel must not write the page table or those cached rows. */
 };
 
 const char* qic_status_string(int status);
@@ -123,7 +129,8 @@ typedef struct qic_decode_args {
   void* workspace;          /* scratch from the caller, zeroed once by qic_workspace_init */
   size_t workspace_bytes;
   int32_t num_splits;       /* KV splits per kv head; 0 = chosen from the SM count */
-  int32_t reserved;
+  int32_t cluster_size;     /* splits merged on chip per thread-block cluster (1..16, divides
+                               num_splits); 0 = chosen with num_splits */
 } qic_decode_args;
 
 /* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len). */
@@ -140,6 +147,55 @@ int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status);
  * Replaces launch_flash_attention / launch_paged_attention (include/kernels.cuh:15-19)
  * and, with flags, the block src/model.cpp:633-652. */
 int qic_decode_attention(const qic_decode_args* args, qic_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Batched paged decode over one shared page pool.                            */
+/* ------------------------------------------------------------------------- */
+
+typedef struct qic_batch_decode_args {
+  int32_t dtype;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t batch;              /* B sequences */
+  int32_t page_size;          /* P, multiple of 8 */
+  int64_t cache_tokens;       /* token rows in the shared pool */
+  int32_t max_pages_per_seq;  /* row length of block_tables */
+  uint32_t flags;             /* QIC_FUSE_*, QIC_PDL; the append goes to position seq_len-1 of each sequence */
+  const void* q;              /* [B, H, d] */
+  void* k_cache;              /* pool [cache_tokens, Hkv, d] */
+  void* v_cache;
+  const int32_t* block_tables;/* [B, max_pages_per_seq] */
+  const void* gate;           /* [B, H, d] or NULL */
+  void* out;                  /* [B, H, d] */
+  float eps;
+  float rope_theta;
+  const void* q_norm_w;       /* [d] */
+  const void* k_norm_w;       /* [d] */
+  const void* k_new;          /* [B, Hkv, d] */
+  const void* v_new;          /* [B, Hkv, d] */
+  const void* plan;           /* device copy of the work items written by qic_batch_plan */
+  int32_t plan_items;
+  int32_t reserved;
+  void* workspace;            /* >= the bytes qic_batch_plan reported, zeroed once by qic_workspace_init */
+  size_t workspace_bytes;
+} qic_batch_decode_args;
+
+/* Bytes of one plan work item. */
+#define QIC_PLAN_ITEM_BYTES 32
+
+/* Host-side planner. seq_lens[b] (host memory) is the number of tokens sequence b
+ * attends (position+1 when appending). Cuts every (sequence, kv head) into work items of
+ * at most ~total/(target_ctas) pipeline stages, ordered longest first, and writes them to
+ * `plan` (host memory, max_items * QIC_PLAN_ITEM_BYTES bytes). target_ctas 0 picks
+ * 16 x the SM count. Returns the item count and the workspace size the plan needs. */
+int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
+                   int target_ctas, void* plan, int max_items, int* items, size_t* workspace_bytes);
+
+/* out[b] = decode attention of sequence b over its block-table row, for all b, in one
+ * launch (with the fused prologue/append/gate options of qic_decode_attention).
+ * Replaces one launch_paged_attention per sequence (include/kernels.cuh:17-19). */
+int qic_batch_decode_attention(const qic_batch_decode_args* args, qic_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* Qwen3.5 GatedDeltaNet decode step (state resident on the device).          */

@@ -27,7 +27,9 @@ from .abi import (  # noqa: F401
     lib_path,
 )
 from .ops import (  # noqa: F401
+    BatchPlan,
     Workspace,
+    batch_decode_attention,
     decode_attention,
     gated_delta_decode,
     kv_append,
@@ -43,7 +45,9 @@ __all__ = [
     "QIC_DTYPE_F16",
     "QIC_FUSE_APPEND",
     "QIC_FUSE_Q_PROLOGUE",
+    "BatchPlan",
     "DecodeArgs",
+    "batch_decode_attention",
     "GdnArgs",
     "QicError",
     "Workspace",

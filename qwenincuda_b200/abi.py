@@ -12,6 +12,8 @@ QIC_FUSE_APPEND = 2
 QIC_DEV_TIMEOUT = 1
 QIC_DEV_BAD_PAGE = 2
 QIC_DEV_PEER_TIMEOUT = 4
+QIC_DEV_BAD_PLAN = 8
+QIC_PDL = 4
 
 STATUS_NAMES = {
     0: "QIC_SUCCESS",
@@ -69,8 +71,44 @@ class DecodeArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("num_splits", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("cluster_size", ctypes.c_int32),
     ]
+
+
+class BatchDecodeArgs(ctypes.Structure):
+    """Mirror of qic_batch_decode_args."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("cache_tokens", ctypes.c_int64),
+        ("max_pages_per_seq", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("q", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("gate", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+        ("q_norm_w", ctypes.c_void_p),
+        ("k_norm_w", ctypes.c_void_p),
+        ("k_new", ctypes.c_void_p),
+        ("v_new", ctypes.c_void_p),
+        ("plan", ctypes.c_void_p),
+        ("plan_items", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+QIC_PLAN_ITEM_BYTES = 32
 
 
 class GdnArgs(ctypes.Structure):
@@ -122,6 +160,12 @@ SIGNATURES = {
     "qic_workspace_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int)]),
     "qic_decode_attention": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
     "qic_gated_delta_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), _vp]),
+    "qic_batch_plan": (
+        ctypes.c_int,
+        [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
+         ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "qic_batch_decode_attention": (ctypes.c_int, [ctypes.POINTER(BatchDecodeArgs), _vp]),
 }
 
 _LIB: ctypes.CDLL | None = None
@@ -134,7 +178,7 @@ def lib() -> ctypes.CDLL:
         path = lib_path()
         if not path.exists():
             raise ImportError(f"{path} is missing; build it with `python -m qwenincuda_b200.build`")
-        handle = ctypes.CDLL(str(path), mode=ctypes.RTLD_GLOBAL)
+        handle = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.restype = res

@@ -74,7 +74,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
                 sys.stdout.write(r.stdout + r.stderr)
             relink = True
     if relink or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB)]
+        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-Xlinker", "-Bsymbolic", *map(str, objs), "-o", str(LIB)]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

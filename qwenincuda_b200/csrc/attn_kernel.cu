@@ -4,29 +4,40 @@
 // of the QweninCuda project): ctx[h] = softmax_t(q_h . K[t, h/g] / sqrt(d)) V[t, h/g].
 //
 // Design
-//  * grid = (splits, kv heads). A CTA owns one kv head and a contiguous range of
-//    32-token stages, and serves every query head of the GQA group, so each K/V
-//    byte is read from HBM once.
-//  * One producer warp streams K and V stages into a shared-memory ring with 2D
-//    TMA tile loads (box = 64 elements x box_h tokens, 128-byte swizzle,
-//    evict-first L2 policy). Paged layouts are gathered by issuing one box per
-//    page segment at the physical row page_table[t/P]*P + t%P; the page-table
-//    window is prefetched one window ahead.
-//  * Four consumer warps take whole stages round-robin. Scores are computed as
-//    S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query-head columns), the
-//    online softmax runs in the exp2 domain on the accumulator fragments, P^T is
-//    turned into the B operand with movmatrix, and O^T += V^T P accumulates in
-//    registers.
-//  * Optionally fused: the q prologue (head RMSNorm + RoPE of q) and the K/V append
-//    of the new token (head RMSNorm + RoPE of k, written straight into its page
-//    slot before the producer loads that stage), and the sigmoid output gate.
-//  * Splits write (lse, o) partials to the caller's workspace; the last CTA of a kv
-//    head (atomic counter) merges them by log-sum-exp and writes the output.
-//  * Every wait is bounded (see ptx.cuh); on timeout the CTA records
-//    QIC_DEV_TIMEOUT, waits (bounded) for its own copies in flight and exits.
+//  * A CTA owns one kv head of one sequence and a contiguous range of pipeline
+//    stages (32 tokens, 16 at head_dim 256), and serves every query head of the GQA
+//    group, so each K/V byte is read from HBM once. Single-sequence launches use a
+//    (splits, kv heads) grid; batched launches read one WorkItem per CTA.
+//  * Two producer warps (one issues the K copies, one the V copies) stream stages
+//    into a 4-stage (64 KB) shared-memory ring with 2D TMA tile loads (box = 64
+//    elements x box_h tokens, 128-byte swizzle, evict-first L2 policy), one copy per
+//    lane. Measured on B200, TMA issue throughput is capped per issuing warp (~24
+//    GB/s with 16-token boxes, independent of ring depth), so a CTA uses two issuing
+//    warps and two CTAs fit per SM. Paged layouts are gathered with one box per page
+//    segment at row page_table[t/P]*P + t%P; two 32-entry windows of the table are
+//    kept in registers and refilled one window ahead.
+//  * Four consumer warps own fixed ring slots (ring depth is a multiple of four, so
+//    a slot is always waited on by the same warp and mbarrier parities cannot
+//    alias). Scores are S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query-head
+//    columns); the online softmax runs in the exp2 domain on the fragments; P^T is
+//    turned into the B operand with movmatrix; O^T += V^T P accumulates in registers.
+//  * Fused options: the q prologue (head RMSNorm + RoPE of q), the K/V append of the
+//    new token (head RMSNorm + RoPE of k written into its page slot before the
+//    producer loads that stage), and the sigmoid output gate.
+//  * The splits of a kv head form thread-block clusters. Each CTA leaves its (o, lse)
+//    partial in shared memory; after a cluster barrier every CTA merges one slice of
+//    the outputs from all partials of its cluster through distributed shared memory.
+//    When a kv head spans several clusters, each cluster slice is written to the
+//    caller's workspace and the last arriving CTA of that slice (release/acquire
+//    counter) merges the cluster partials by log-sum-exp.
+//  * Programmatic dependent launch (QIC_PDL): the CTA signals its dependents at
+//    start and reads its inputs, the append slot and the workspace only after
+//    griddepcontrol.wait, so the next call's K/V prefetch overlaps this call's tail.
+//  * Every wait is bounded (ptx.cuh); on timeout the CTA records QIC_DEV_TIMEOUT,
+//    drains its own copies (bounded) and exits.
 //
-// This translation unit is compiled with --use_fast_math so that the fused norm /
-// RoPE / gate arithmetic matches the reference build bit for bit.
+// Compiled with --use_fast_math so the fused norm / RoPE / gate arithmetic matches
+// the reference build bit for bit.
 #include "qic_internal.h"
 #include "rowops.cuh"
 
@@ -34,25 +45,71 @@ namespace qic {
 
 template <int D>
 struct AttnShape {
-  static constexpr int kChunks = D / 64;                       // 128-byte rows per token row
-  static constexpr int kKBytes = kStageTokens * D * 2;         // K bytes of one stage
-  static constexpr int kStageBytes = 2 * kKBytes;              // K + V
-  static constexpr int kRing = (D == 256) ? 6 : ((D == 128) ? 12 : 24);
-  static constexpr int kRingBytes = kRing * kStageBytes;       // 192 KiB
-  static constexpr int kCtrlBytes = 8 * (2 * kRing + 2);       // full[], empty[], append barrier, pad
+  static constexpr int kTok = stage_tokens(D);                 // tokens per stage
+  static constexpr int kGroups = kTok / 16;                     // 16-token mma groups per stage
+  static constexpr int kChunks = D / 64;                        // 128-byte rows per token row
+  static constexpr int kKBytes = kTok * D * 2;                  // K bytes of one stage
+  static constexpr int kStageBytes = 2 * kKBytes;               // K + V
+  static constexpr int kRing = (D == 64) ? 8 : 4;
+  static_assert(kRing % kConsumerWarps == 0, "a ring slot must always be consumed by the same warp");
+  static constexpr int kRingBytes = kRing * kStageBytes;        // 64 KB
+  static constexpr int kCombineBytes = kConsumerWarps * (kMaxGroup * D + 2 * kMaxGroup) * 4;
+  static_assert(kCombineBytes + (kMaxGroup * (D + 1) + 4) * 4 <= kRingBytes, "combine buffer + partial");
+  static constexpr int kCtrlBytes = 8 * (2 * kRing + 2);        // full[], empty[], append barrier, pad
   static constexpr int kQBytes = kMaxGroup * D * 2;
   static constexpr int kFlagBytes = 64;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes;
 };
 
 __device__ __forceinline__ void consumer_sync() {
+  __syncwarp();
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
 
+// Cluster barrier; every thread of every CTA in the cluster executes it the same
+// number of times (consumers and producers alike).
+// The non-.aligned form is used: each thread arrives on its own, so a warp that has
+// not reconverged after a divergent loop cannot complete the barrier early.
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Generic address of the same shared-memory variable in CTA `rank` of this cluster.
+template <typename X>
+__device__ __forceinline__ X* cluster_map(X* p, int rank) {
+  uint64_t out;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<X*>(out);
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
+// out = T(o), then the optional sigmoid gate as the reference applies it.
+template <typename T>
+__device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, float o) {
+  T ot = from_f32<T>(o);
+  if (gb != nullptr) {
+    const float g = to_f32<T>(gb[i]);
+    const float sig = 1.0f / (1.0f + expf(-g));
+    ot = from_f32<T>(to_f32<T>(ot) * sig);
+  }
+  ob[i] = ot;
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __grid_constant__ AttnParams p) {
   using Sh = AttnShape<D>;
   constexpr int kRing = Sh::kRing;
+  constexpr int TOK = Sh::kTok;
+  constexpr int NG = Sh::kGroups;
   constexpr int KS = D / 16;  // k-steps of 16 dims / m-tiles of 16 dims
 
   extern __shared__ uint8_t smem_dyn[];
@@ -63,56 +120,85 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
   uint64_t* append_bar = empty + kRing;
   T* q_s = reinterpret_cast<T*>(ring + Sh::kRingBytes + Sh::kCtrlBytes);
   volatile int* flags_s = reinterpret_cast<volatile int*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes);
-  // flags_s[0]: abort, flags_s[1]: this CTA merges, flags_s[2]: stages issued (producer)
+  // flags_s[0]: abort, flags_s[1]: this CTA merges
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y;
-  const int nsplit = p.n_splits;
-  const int st_lo = static_cast<int>(static_cast<long long>(split) * p.n_stages / nsplit);
-  const int st_hi = static_cast<int>(static_cast<long long>(split + 1) * p.n_stages / nsplit);
+
+  // ---- this CTA's unit of work ----
+  int b, kvh, split, nsplit, st_lo, st_hi, S, part_base;
+  if (p.plan != nullptr) {
+    const WorkItem w = p.plan[blockIdx.x];
+    b = w.b;
+    kvh = w.kvh;
+    split = w.split;
+    nsplit = w.nsplit;
+    st_lo = w.st_lo;
+    st_hi = w.st_hi;
+    S = w.seq_len;
+    part_base = w.part_base;
+  } else {
+    b = 0;
+    kvh = blockIdx.y;
+    split = blockIdx.x;
+    nsplit = p.n_splits;
+    S = p.seq_len;
+    st_lo = static_cast<int>(static_cast<long long>(split) * p.n_stages / nsplit);
+    st_hi = static_cast<int>(static_cast<long long>(split + 1) * p.n_stages / nsplit);
+    part_base = kvh * (nsplit / p.cluster);  // one global slot per cluster
+  }
+  if (p.cluster == 1 && nsplit > 1 &&
+      (part_base + split >= p.part_slots || b * p.Hkv + kvh >= p.num_counters || nsplit > kMaxSplits)) {
+    // a planned work item that does not fit the workspace is reported, not executed
+    // (cluster launches are shaped on the host and never take this exit)
+    if (threadIdx.x == 0) record_status(p.status, QIC_DEV_BAD_PLAN);
+    return;
+  }
   const int nst = st_hi - st_lo;
-  const int S = p.seq_len;
+  const int n_stages_seq = (S + TOK - 1) / TOK;
   const int G = p.G;
-  const bool do_append = (p.flags & QIC_FUSE_APPEND) && st_hi == p.n_stages;
+  const bool do_append = (p.flags & QIC_FUSE_APPEND) && st_hi == n_stages_seq;
+  const int32_t* table = p.page_table != nullptr ? p.page_table + static_cast<size_t>(b) * p.table_bstride : nullptr;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
     for (int i = 0; i < kRing; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], kProducerWarps);
       mbar_init(&empty[i], 1);
     }
     mbar_init(append_bar, 1);
     flags_s[0] = 0;
     flags_s[1] = 0;
-    flags_s[2] = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
-    // ======================= producer warp =======================
+  if (warp >= kConsumerWarps) {
+    // ======================= producer warps =======================
+    // warp kConsumerWarps issues the K copies of every stage, the next warp the V copies
+    const int pw = warp - kConsumerWarps;
     const uint64_t pol = l2_policy_evict_first();
-    if (lane == 0) {
-      tma_prefetch_desc(&p.tm_k);
-      tma_prefetch_desc(&p.tm_v);
-    }
-    const bool paged = p.page_table != nullptr;
+    if (lane == 0) tma_prefetch_desc(pw == 0 ? &p.tm_k : &p.tm_v);
+    const CUtensorMap* tmap = pw == 0 ? &p.tm_k : &p.tm_v;
     const int bh = p.box_h;
-    const int box_row_bytes = bh * 128;   // one 64-element chunk of bh token rows
-    const int box_bytes = bh * D * 2;     // all chunks of bh token rows
+    const int box_row_bytes = bh * 128;  // one 64-element chunk of bh token rows
+    const int box_bytes = bh * D * 2;    // all chunks of bh token rows
     const int P = p.page_size;
-    const int npages = paged ? (S + P - 1) / P : 0;
-    // page-table window: lane l holds entry wbase + l; `nxt` holds the next window
+    const int npages = table != nullptr ? (S + P - 1) / P : 0;
+    // page-table windows: lane l holds entry wbase + l in `cur` and wbase + 32 + l in `nxt`
     int wbase = 0, cur = 0, nxt = 0;
-    if (paged) {
-      wbase = (st_lo * kStageTokens) / P;
-      int e0 = wbase + lane, e1 = wbase + 32 + lane;
-      cur = e0 < npages ? __ldg(p.page_table + e0) : 0;
-      nxt = e1 < npages ? __ldg(p.page_table + e1) : 0;
+    if (table != nullptr) {
+      wbase = (st_lo * TOK) / P;
+      const int e0 = wbase + lane, e1 = wbase + 32 + lane;
+      cur = e0 < npages ? __ldg(table + e0) : 0;
+      nxt = e1 < npages ? __ldg(table + e1) : 0;
     }
+    // lane -> (box, chunk) of this warp's copies of a stage
+    const int op_box = lane / Sh::kChunks;
+    const int op_chunk = lane % Sh::kChunks;
+    const int kv_off = pw * Sh::kKBytes;
     int issued = 0;
     bool ok = true;
 #pragma unroll 1
@@ -128,8 +214,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
         ok = false;
         break;
       }
-      const int t0 = (st_lo + i) * kStageTokens;
-      const int nvalid = min(kStageTokens, S - t0);
+      const int t0 = (st_lo + i) * TOK;
+      const int nvalid = min(TOK, S - t0);
       if (do_append && i == nst - 1) {
         // the stage holding the new token is loaded after the append has landed
         if (!__all_sync(kFullMask, mbar_wait(append_bar, 0, deadline))) {
@@ -138,49 +224,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
         }
       }
       const int nbox = (nvalid + bh - 1) / bh;
+      const int nops = nbox * Sh::kChunks;  // copies of this warp
+      const int jb = min(op_box, nbox - 1);
+      const int tb = t0 + jb * bh;
+      int row = tb;
+      if (table != nullptr) {
+        const int e_first = t0 / P;
+        while (e_first >= wbase + 32) {  // uniform across the warp
+          cur = nxt;
+          wbase += 32;
+          const int en = wbase + 32 + lane;
+          nxt = en < npages ? __ldg(table + en) : 0;
+        }
+        const int e = tb / P;
+        const int src = e - wbase;  // < 64: a stage spans at most 5 pages of >= 8 tokens
+        const int v0 = __shfl_sync(kFullMask, cur, src & 31);
+        const int v1 = __shfl_sync(kFullMask, nxt, src & 31);
+        const int page = src < 32 ? v0 : v1;
+        long long r = static_cast<long long>(page) * P + (tb - e * P);
+        if (lane < nops && (page < 0 || (p.cache_tokens > 0 && r + bh > p.cache_tokens))) {
+          record_status(p.status, QIC_DEV_BAD_PAGE);
+          r = tb - e * P;  // clamp to page 0
+        }
+        row = static_cast<int>(r);
+      }
       uint8_t* sk = ring + slot * Sh::kStageBytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * box_bytes * 2));
-#pragma unroll 1
-      for (int j = 0; j < nbox; ++j) {
-        const int tb = t0 + j * bh;
-        int row = tb;
-        if (paged) {
-          const int e = tb / P;
-          while (e >= wbase + 32) {  // uniform across the warp
-            cur = nxt;
-            wbase += 32;
-            const int en = wbase + 32 + lane;
-            nxt = en < npages ? __ldg(p.page_table + en) : 0;
-          }
-          const int page = __shfl_sync(kFullMask, cur, e - wbase);
-          long long r = static_cast<long long>(page) * P + (tb - e * P);
-          if (page < 0 || (p.cache_tokens > 0 && r + bh > p.cache_tokens)) {
-            if (lane == 0) record_status(p.status, QIC_DEV_BAD_PAGE);
-            r = tb - e * P;  // clamp to page 0
-          }
-          row = static_cast<int>(r);
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int c = 0; c < Sh::kChunks; ++c) {
-            uint8_t* dst = sk + j * box_bytes + c * box_row_bytes;
-            const int x = kvh * D + c * 64;
-            tma_load_2d(dst, &p.tm_k, &full[slot], x, row, pol);
-            tma_load_2d(dst + Sh::kKBytes, &p.tm_v, &full[slot], x, row, pol);
-          }
-        }
+      // each producer warp posts the bytes of its own copies before issuing them
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * box_bytes));
+      __syncwarp();
+      if (lane < nops) {
+        uint8_t* dst = sk + kv_off + op_box * box_bytes + op_chunk * box_row_bytes;
+        tma_load_2d(dst, tmap, &full[slot], kvh * D + op_chunk * 64, row, pol);
       }
       issued = i + 1;
       __syncwarp();
     }
-    if (!ok) {
-      if (lane == 0) {
-        record_status(p.status, QIC_DEV_TIMEOUT);
-        flags_s[0] = 1;
-        // wait (bounded) for the copies this CTA still has in flight
-        const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
-        for (int i = max(0, issued - kRing); i < issued; ++i) mbar_wait(&full[i % kRing], (i / kRing) & 1, dl2);
-      }
+    if (!ok && lane == 0) {
+      record_status(p.status, QIC_DEV_TIMEOUT);
+      flags_s[0] = 1;
+      // wait (bounded) for the copies this CTA still has in flight
+      const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
+      for (int i = max(0, issued - kRing); i < issued; ++i) mbar_wait(&full[i % kRing], (i / kRing) & 1, dl2);
+    }
+    __syncwarp();
+    if (nsplit > 1) {
+      // every thread of the cluster takes part in the consumers' two cluster barriers
+      cluster_sync_all();
+      cluster_sync_all();
     }
     return;
   }
@@ -188,6 +278,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
   // ======================= consumer warps =======================
   const int ctid = threadIdx.x;  // 0..127
   const int hd = p.head_dim;
+  const T* qb = static_cast<const T*>(p.q) + static_cast<size_t>(b) * p.q_bstride;
+  const T* gb = p.gate != nullptr ? static_cast<const T*>(p.gate) + static_cast<size_t>(b) * p.q_bstride : nullptr;
+  T* ob = static_cast<T*>(p.out) + static_cast<size_t>(b) * p.q_bstride;
+  // inputs written by the preceding kernel are read only after it has completed
+  pdl_wait();
   // ---- prologue: q rows into shared memory, and the fused append ----
   {
     const int nrows = G + (do_append ? 1 : 0);
@@ -195,8 +290,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     for (int r = warp; r < nrows; r += kConsumerWarps) {
       float v[D / 32];
       if (r < G) {
-        const int h = kvh * G + r;
-        row_load<T, D>(static_cast<const T*>(p.q) + static_cast<size_t>(h) * D, v, lane);
+        row_load<T, D>(qb + static_cast<size_t>(kvh * G + r) * D, v, lane);
         if (p.flags & QIC_FUSE_Q_PROLOGUE) {
           row_rmsnorm<T, D>(v, static_cast<const T*>(p.q_norm_w), hd, p.eps, lane);
           row_rope<T, D>(v, hd, S - 1, p.theta, lane);
@@ -206,21 +300,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
         // K/V append at position S-1 (src/model.cpp:634,637,639-641)
         const int pos = S - 1;
         long long slot = pos;
-        if (p.page_table != nullptr) {
+        if (table != nullptr) {
           const int e = pos / p.page_size;
-          slot = static_cast<long long>(__ldg(p.page_table + e)) * p.page_size + (pos - e * p.page_size);
+          slot = static_cast<long long>(__ldg(table + e)) * p.page_size + (pos - e * p.page_size);
         }
         const size_t kv_dim = static_cast<size_t>(p.Hkv) * D;
+        const size_t nb = static_cast<size_t>(b) * p.kv_new_bstride + static_cast<size_t>(kvh) * D;
         if (slot >= 0 && slot < p.cache_tokens) {
-          row_load<T, D>(static_cast<const T*>(p.k_new) + static_cast<size_t>(kvh) * D, v, lane);
+          row_load<T, D>(static_cast<const T*>(p.k_new) + nb, v, lane);
+          float vv[D / 32];
+          row_load<T, D>(static_cast<const T*>(p.v_new) + nb, vv, lane);
           row_rmsnorm<T, D>(v, static_cast<const T*>(p.k_norm_w), hd, p.eps, lane);
           row_rope<T, D>(v, hd, pos, p.theta, lane);
-          T* kdst = static_cast<T*>(p.k_cache) + static_cast<size_t>(slot) * kv_dim + static_cast<size_t>(kvh) * D;
-          row_store<T, D>(kdst, v, lane);
-          float vv[D / 32];
-          row_load<T, D>(static_cast<const T*>(p.v_new) + static_cast<size_t>(kvh) * D, vv, lane);
-          T* vdst = static_cast<T*>(p.v_cache) + static_cast<size_t>(slot) * kv_dim + static_cast<size_t>(kvh) * D;
-          row_store<T, D>(vdst, vv, lane);
+          const size_t at = static_cast<size_t>(slot) * kv_dim + static_cast<size_t>(kvh) * D;
+          row_store<T, D>(static_cast<T*>(p.k_cache) + at, v, lane);
+          row_store<T, D>(static_cast<T*>(p.v_cache) + at, vv, lane);
         } else if (lane == 0) {
           record_status(p.status, QIC_DEV_BAD_PAGE);
         }
@@ -233,8 +327,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
   consumer_sync();
 
   // ---- B fragments of Q^T (k = dims, n = query heads of the group) ----
-  const int hq = lane >> 2;         // n index held by this lane in B fragments
-  const int kq = (lane & 3) * 2;    // k pair held by this lane
+  const int hq = lane >> 2;       // n index held by this lane in B fragments
+  const int kq = (lane & 3) * 2;  // k pair held by this lane
   uint32_t qf[KS][2];
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks) {
@@ -252,11 +346,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
   const int lbh = p.log2_box_h;
   const int box_bytes = bh * D * 2;
   const int box_row_bytes = bh * 128;
-  const int q8 = lane >> 3;   // ldmatrix matrix index supplied by this lane
-  const int rr = lane & 7;    // row within that 8x8 matrix
-  uint32_t rowK[2], rowV[2];
+  const int q8 = lane >> 3;  // ldmatrix matrix index supplied by this lane
+  const int rr = lane & 7;   // row within that 8x8 matrix
+  uint32_t rowK[NG], rowV[NG];
 #pragma unroll
-  for (int g2 = 0; g2 < 2; ++g2) {
+  for (int g2 = 0; g2 < NG; ++g2) {
     const int tk = g2 * 16 + (q8 & 1) * 8 + rr;
     const int tv = g2 * 16 + (q8 >> 1) * 8 + rr;
     rowK[g2] = static_cast<uint32_t>((tk >> lbh) * box_bytes + (tk & (bh - 1)) * 128);
@@ -279,16 +373,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
       ok = false;
       break;
     }
-    const int t0 = (st_lo + i) * kStageTokens;
-    const int nvalid = min(kStageTokens, S - t0);
+    const int t0 = (st_lo + i) * TOK;
+    const int nvalid = min(TOK, S - t0);
     uint8_t* sk = ring + slot * Sh::kStageBytes;
     const uint32_t bk = smem_u32(sk);
     const uint32_t bv = bk + Sh::kKBytes;
-    if (nvalid < kStageTokens) {
+    if (nvalid < TOK) {
       // rows past the sequence end hold stale or unloaded data: zero V there so
       // P = 0 rows cannot turn into NaN in the PV product
       uint8_t* sv = sk + Sh::kKBytes;
-      const int nz = (kStageTokens - nvalid) * Sh::kChunks * 8;  // 16-byte units
+      const int nz = (TOK - nvalid) * Sh::kChunks * 8;  // 16-byte units
       for (int u = lane; u < nz; u += 32) {
         const int t = nvalid + u / (Sh::kChunks * 8);
         const int rem = u % (Sh::kChunks * 8);
@@ -301,10 +395,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
       __syncwarp();
     }
 
-    // S^T = K Q^T for the two 16-token groups of the stage
-    float sc[2][4];
+    // S^T = K Q^T for each 16-token group of the stage
+    float sc[NG][4];
 #pragma unroll
-    for (int g2 = 0; g2 < 2; ++g2) {
+    for (int g2 = 0; g2 < NG; ++g2) {
       sc[g2][0] = sc[g2][1] = sc[g2][2] = sc[g2][3] = 0.0f;
       if (g2 * 16 < nvalid) {
 #pragma unroll
@@ -320,7 +414,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     // scale, mask, online softmax (per head column)
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int g2 = 0; g2 < 2; ++g2) {
+    for (int g2 = 0; g2 < NG; ++g2) {
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int t = g2 * 16 + hq + r * 8;
@@ -344,7 +438,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     m1 = mn1;
     float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
-    for (int g2 = 0; g2 < 2; ++g2) {
+    for (int g2 = 0; g2 < NG; ++g2) {
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         sc[g2][2 * r + 0] = exp2f(sc[g2][2 * r + 0] - mu0);
@@ -364,7 +458,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     }
     // O^T += V^T P
 #pragma unroll
-    for (int g2 = 0; g2 < 2; ++g2) {
+    for (int g2 = 0; g2 < NG; ++g2) {
       if (g2 * 16 < nvalid) {
         const uint32_t b0 = movmatrix_trans(pack2<T>(sc[g2][0], sc[g2][1]));
         const uint32_t b1 = movmatrix_trans(pack2<T>(sc[g2][2], sc[g2][3]));
@@ -381,11 +475,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  if (!ok) {
-    if (lane == 0) {
-      record_status(p.status, QIC_DEV_TIMEOUT);
-      flags_s[0] = 1;
-    }
+  if (!ok && lane == 0) {
+    record_status(p.status, QIC_DEV_TIMEOUT);
+    flags_s[0] = 1;
   }
   // full row sums per head column
 #pragma unroll
@@ -394,13 +486,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     l1 += __shfl_xor_sync(kFullMask, l1, o);
   }
   consumer_sync();
-  if (flags_s[0]) return;  // aborted: the producer drains its copies
+  const bool aborted = flags_s[0] != 0;
 
   // ---- combine the four consumer warps (ring memory is free now) ----
-  float* cm = reinterpret_cast<float*>(ring);         // [4][8] m
-  float* cl = cm + kConsumerWarps * 8;                // [4][8] l
-  float* co = cl + kConsumerWarps * 8;                // [4][8][D] o
-  {
+  float* cm = reinterpret_cast<float*>(ring);  // [4][8] m
+  float* cl = cm + kConsumerWarps * 8;         // [4][8] l
+  float* co = cl + kConsumerWarps * 8;         // [4][8][D] o
+  float* mine = reinterpret_cast<float*>(ring + Sh::kCombineBytes);  // this split: [o: G*D][lse: G]
+  if (!aborted) {
     const int hA = (lane & 3) * 2, hB = hA + 1;
     if (lane < 4) {
       cm[warp * 8 + hA] = m0;
@@ -418,87 +511,105 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
     }
   }
   consumer_sync();
-
   const size_t qoff = static_cast<size_t>(kvh) * G * D;  // first output row of this group
-  const int pf = partial_floats(G, D);
-  float* mypart = p.part + (static_cast<size_t>(kvh) * nsplit + split) * pf;
+  const int GD = G * D;
+  if (!aborted) {
 #pragma unroll 1
-  for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {
-    const int h = idx / D, d = idx - (idx / D) * D;
-    float M = -INFINITY;
+    for (int idx = ctid; idx < GD; idx += kConsumerWarps * 32) {
+      const int h = idx / D;
+      float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cm[w * 8 + h]);
-    const float Mu = (M == -INFINITY) ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cm[w * 8 + h]);
+      const float Mu = (M == -INFINITY) ? 0.0f : M;
+      float L = 0.0f, O = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float wt = exp2f(cm[w * 8 + h] - Mu);
-      L += cl[w * 8 + h] * wt;
-      O += co[(w * 8 + h) * D + d] * wt;
-    }
-    if (nsplit == 1) {
-      const float inv_l = 1.0f / fmaxf(L, 1e-12f);
-      T ot = from_f32<T>(O * inv_l);
-      if (p.gate != nullptr) {
-        const float g = to_f32<T>(static_cast<const T*>(p.gate)[qoff + idx]);
-        const float sig = 1.0f / (1.0f + expf(-g));
-        ot = from_f32<T>(to_f32<T>(ot) * sig);
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float wt = exp2f(cm[w * 8 + h] - Mu);
+        L += cl[w * 8 + h] * wt;
+        O += co[(w * 8 + h) * D + (idx - h * D)] * wt;
       }
-      static_cast<T*>(p.out)[qoff + idx] = ot;
-    } else {
-      mypart[G + idx] = (L > 0.0f) ? O / L : 0.0f;
-      if (d == 0) mypart[h] = (L > 0.0f) ? Mu + log2f(L) : -INFINITY;
+      if (nsplit == 1) {
+        const float inv_l = 1.0f / fmaxf(L, 1e-12f);
+        T ot = from_f32<T>(O * inv_l);
+        if (gb != nullptr) {
+          const float g = to_f32<T>(gb[qoff + idx]);
+          const float sig = 1.0f / (1.0f + expf(-g));
+          ot = from_f32<T>(to_f32<T>(ot) * sig);
+        }
+        ob[qoff + idx] = ot;
+      } else {
+        mine[idx] = (L > 0.0f) ? O / L : 0.0f;
+        if (idx - h * D == 0) mine[GD + h] = (L > 0.0f) ? Mu + log2f(L) : -INFINITY;
+      }
     }
   }
   if (nsplit == 1) return;
 
-  // ---- cross-split merge by the last CTA of this kv head ----
-  __threadfence();
-  consumer_sync();
-  if (ctid == 0) {
-    const int prev = atomicAdd(p.counters + kvh, 1);
-    flags_s[1] = (prev == nsplit - 1) ? 1 : 0;
-  }
-  consumer_sync();
-  if (!flags_s[1]) return;
-  __threadfence();
-  float* lse_s = reinterpret_cast<float*>(ring);  // [G] merged lse
-  const float* gpart = p.part + static_cast<size_t>(kvh) * nsplit * pf;
-  {
+  // ---- merge the partials of this cluster through distributed shared memory ----
+  cluster_sync_all();  // every CTA of the cluster has its partial in shared memory
+  const int C = p.cluster;
+  const int rank = split % C;
+  const int cid = split / C;
+  const int nclust = nsplit / C;
+  const int slice = (GD + C - 1) / C;
+  const int lo = rank * slice;
+  const int hi = min(GD, lo + slice);
+  float* gslot = p.part + static_cast<size_t>(part_base + cid) * partial_floats(G, D);  // [o: G*D][lse: G]
 #pragma unroll 1
-    for (int h = warp; h < G; h += kConsumerWarps) {
-      float mx = -INFINITY;
-      for (int s = lane; s < nsplit; s += 32) mx = fmaxf(mx, __ldcg(gpart + static_cast<size_t>(s) * pf + h));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
-      const float mxu = (mx == -INFINITY) ? 0.0f : mx;
-      float sum = 0.0f;
-      for (int s = lane; s < nsplit; s += 32) sum += exp2f(__ldcg(gpart + static_cast<size_t>(s) * pf + h) - mxu);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
-      if (lane == 0) lse_s[h] = (sum > 0.0f) ? mxu + log2f(sum) : 0.0f;
-    }
-  }
-  consumer_sync();
-#pragma unroll 1
-  for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {
+  for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
     const int h = idx / D;
-    const float lse = lse_s[h];
-    float o = 0.0f;
-#pragma unroll 4
-    for (int s = 0; s < nsplit; ++s) {
-      const float* ps = gpart + static_cast<size_t>(s) * pf;
-      o += __ldcg(ps + G + idx) * exp2f(__ldcg(ps + h) - lse);
+    float lse_c[kMaxCluster];
+    float mx = -INFINITY;
+    for (int c = 0; c < C; ++c) {
+      lse_c[c] = *cluster_map(mine + GD + h, c);
+      mx = fmaxf(mx, lse_c[c]);
     }
-    T ot = from_f32<T>(o);
-    if (p.gate != nullptr) {
-      const float g = to_f32<T>(static_cast<const T*>(p.gate)[qoff + idx]);
-      const float sig = 1.0f / (1.0f + expf(-g));
-      ot = from_f32<T>(to_f32<T>(ot) * sig);
+    const float mxu = (mx == -INFINITY) ? 0.0f : mx;
+    float sum = 0.0f, o = 0.0f;
+    for (int c = 0; c < C; ++c) {
+      const float w = exp2f(lse_c[c] - mxu);
+      sum += w;
+      o += w * *cluster_map(mine + idx, c);
     }
-    static_cast<T*>(p.out)[qoff + idx] = ot;
+    o = sum > 0.0f ? o / sum : 0.0f;
+    if (nclust == 1) {
+      write_out<T>(ob, gb, qoff + idx, o);
+    } else {
+      gslot[idx] = o;
+      if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
+    }
   }
-  if (ctid == 0) p.counters[kvh] = 0;  // ready for the next call
+  if (nclust > 1) {
+    // ---- merge the cluster partials of this slice: last arriving cluster ----
+    consumer_sync();
+    const int counter = (b * p.Hkv + kvh) * C + rank;
+    if (ctid == 0) {
+      const int prev = atomic_add_acq_rel_gpu(p.counters + counter, 1);
+      flags_s[1] = (prev == nclust - 1) ? 1 : 0;
+    }
+    consumer_sync();
+    if (flags_s[1]) {
+      const float* g0 = p.part + static_cast<size_t>(part_base) * partial_floats(G, D);
+      const int pf = partial_floats(G, D);
+#pragma unroll 1
+      for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
+        const int h = idx / D;
+        float mx = -INFINITY;
+        for (int k = 0; k < nclust; ++k) mx = fmaxf(mx, __ldcg(g0 + static_cast<size_t>(k) * pf + GD + h));
+        const float mxu = (mx == -INFINITY) ? 0.0f : mx;
+        float sum = 0.0f, o = 0.0f;
+        for (int k = 0; k < nclust; ++k) {
+          const float w = exp2f(__ldcg(g0 + static_cast<size_t>(k) * pf + GD + h) - mxu);
+          sum += w;
+          o += w * __ldcg(g0 + static_cast<size_t>(k) * pf + idx);
+        }
+        write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
+      }
+      if (ctid == 0) p.counters[counter] = 0;  // ready for the next call
+    }
+  }
+  // keep this CTA's shared memory alive until every CTA of the cluster has read it
+  cluster_sync_all();
 }
 
 // ----------------------------------------------------------------------------
@@ -514,7 +625,7 @@ size_t decode_attention_smem_bytes(int head_dim) {
 }
 
 template <typename T, int D>
-static cudaError_t launch_typed(const AttnParams& p, cudaStream_t stream) {
+static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t stream) {
   static unsigned long long configured = 0;  // one bit per device ordinal
   const int smem = AttnShape<D>::kSmemBytes;
   int dev = 0;
@@ -522,26 +633,91 @@ static cudaError_t launch_typed(const AttnParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (dev < 64 && !(configured & (1ull << dev))) {
     e = cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured |= 1ull << dev;
   }
-  dim3 grid(p.n_splits, p.Hkv);
-  decode_attn_kernel<T, D><<<grid, kAttnThreads, smem, stream>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (p.flags & QIC_PDL) ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(p.cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, D>, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
-cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream) {
+template <typename T, int D>
+static int max_active_clusters_typed(int cluster) {
+  // cached per device and cluster size: clusters of `cluster` CTAs that fit on the GPU at once
+  static int cache[64][kMaxCluster + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || cluster < 1 || cluster > kMaxCluster) return 0;
+  if (cache[dev][cluster] != 0) return cache[dev][cluster];
+  const int smem = AttnShape<D>::kSmemBytes;
+  if (cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster, 1, 1);
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<T, D>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cache[dev][cluster] = n;
+  return n;
+}
+
+int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster) {
   if (dtype == QIC_DTYPE_BF16) {
     switch (head_dim) {
-      case 64: return launch_typed<__nv_bfloat16, 64>(p, stream);
-      case 128: return launch_typed<__nv_bfloat16, 128>(p, stream);
-      case 256: return launch_typed<__nv_bfloat16, 256>(p, stream);
+      case 64: return max_active_clusters_typed<__nv_bfloat16, 64>(cluster);
+      case 128: return max_active_clusters_typed<__nv_bfloat16, 128>(cluster);
+      case 256: return max_active_clusters_typed<__nv_bfloat16, 256>(cluster);
     }
   } else {
     switch (head_dim) {
-      case 64: return launch_typed<__half, 64>(p, stream);
-      case 128: return launch_typed<__half, 128>(p, stream);
-      case 256: return launch_typed<__half, 256>(p, stream);
+      case 64: return max_active_clusters_typed<__half, 64>(cluster);
+      case 128: return max_active_clusters_typed<__half, 128>(cluster);
+      case 256: return max_active_clusters_typed<__half, 256>(cluster);
+    }
+  }
+  return 0;
+}
+
+cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream) {
+  const dim3 grid = p.plan != nullptr ? dim3(p.n_splits, 1, 1) : dim3(p.n_splits, p.Hkv, 1);
+  if (dtype == QIC_DTYPE_BF16) {
+    switch (head_dim) {
+      case 64: return launch_typed<__nv_bfloat16, 64>(p, grid, stream);
+      case 128: return launch_typed<__nv_bfloat16, 128>(p, grid, stream);
+      case 256: return launch_typed<__nv_bfloat16, 256>(p, grid, stream);
+    }
+  } else {
+    switch (head_dim) {
+      case 64: return launch_typed<__half, 64>(p, grid, stream);
+      case 128: return launch_typed<__half, 128>(p, grid, stream);
+      case 256: return launch_typed<__half, 256>(p, grid, stream);
     }
   }
   return cudaErrorInvalidValue;

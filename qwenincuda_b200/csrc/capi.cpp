@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "qic_internal.h"
 
@@ -166,9 +167,10 @@ int qic_kv_append(int dtype, const void* k_new, const void* v_new, const void* k
 size_t qic_decode_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int max_seq_len) {
   if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_seq_len < 0) return 0;
   const int G = num_heads / num_kv_heads;
-  const int n_stages = (max_seq_len + qic::kStageTokens - 1) / qic::kStageTokens;
-  const int splits = std::max(1, std::min(qic::kMaxSplits, n_stages));
-  return qic::kWsHeader + align256(static_cast<size_t>(num_kv_heads) * sizeof(int)) +
+  const int tok = qic::stage_tokens(head_dim);
+  const int n_stages = (max_seq_len + tok - 1) / tok;
+  const int splits = std::max(1, std::min(qic::kMaxSplits, n_stages));  // bounds cluster partial slots too
+  return qic::kWsPartialOffset +
          static_cast<size_t>(num_kv_heads) * splits * qic::partial_floats(G, head_dim) * sizeof(float);
 }
 
@@ -189,24 +191,75 @@ int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status) 
   return QIC_SUCCESS;
 }
 
+namespace {
+
+// Shared checks of the single and batched decode entry points.
+int check_attention_common(int dtype, int H, int Hkv, int D, uint32_t flags, const void* q, const void* out,
+                           const void* k_cache, const void* v_cache, const void* gate, const void* q_norm_w,
+                           const void* k_norm_w, const void* k_new, const void* v_new, const void* workspace) {
+  if (!valid_dtype(dtype)) return QIC_ERROR_INVALID_VALUE;
+  if (H <= 0 || Hkv <= 0 || H % Hkv != 0 || !q || !out || !k_cache || !v_cache) return QIC_ERROR_INVALID_VALUE;
+  if (!supported_head_dim(D) || H / Hkv > qic::kMaxGroup) return QIC_ERROR_NOT_SUPPORTED;
+  const bool fuse_q = (flags & QIC_FUSE_Q_PROLOGUE) != 0;
+  const bool fuse_app = (flags & QIC_FUSE_APPEND) != 0;
+  if (fuse_q && !q_norm_w) return QIC_ERROR_INVALID_VALUE;
+  if (fuse_app && (!k_new || !v_new || !k_norm_w)) return QIC_ERROR_INVALID_VALUE;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned2(out) || (gate && !aligned2(gate)) ||
+      (fuse_q && !aligned16(q_norm_w)) ||
+      (fuse_app && (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_norm_w))) ||
+      (workspace && !aligned16(workspace)))
+    return QIC_ERROR_MISALIGNED;
+  return QIC_SUCCESS;
+}
+
+void fill_common(qic::AttnParams& p, int H, int Hkv, int D, const void* q, const void* gate, void* out,
+                 void* k_cache, void* v_cache, uint32_t flags, float eps, float theta, const void* q_norm_w,
+                 const void* k_norm_w, const void* k_new, const void* v_new) {
+  p.q = q;
+  p.gate = gate;
+  p.out = out;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.q_norm_w = q_norm_w;
+  p.k_norm_w = k_norm_w;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.G = H / Hkv;
+  p.head_dim = D;
+  p.flags = static_cast<int>(flags & (QIC_FUSE_Q_PROLOGUE | QIC_FUSE_APPEND | QIC_PDL));
+  p.eps = eps;
+  p.theta = theta;
+  p.scale_log2 = static_cast<float>((1.0 / std::sqrt(static_cast<double>(D))) * 1.4426950408889634);
+  p.timeout_ns = timeout_ns();
+}
+
+int box_height(bool paged, int page_size, int tok, int* log2) {
+  int bh = tok;
+  if (paged) {
+    bh = page_size & (-page_size);  // largest power of two dividing P
+    if (bh > tok) bh = tok;
+  }
+  int l = 0;
+  while ((1 << l) < bh) ++l;
+  *log2 = l;
+  return bh;
+}
+
+}  // namespace
+
 int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
-  if (a == nullptr || !valid_dtype(a->dtype)) return QIC_ERROR_INVALID_VALUE;
+  if (a == nullptr) return QIC_ERROR_INVALID_VALUE;
   const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim, S = a->seq_len;
-  if (H <= 0 || Hkv <= 0 || H % Hkv != 0 || S < 0 || !a->q || !a->out || !a->k_cache || !a->v_cache)
-    return QIC_ERROR_INVALID_VALUE;
+  int rc = check_attention_common(a->dtype, H, Hkv, D, a->flags, a->q, a->out, a->k_cache, a->v_cache, a->gate,
+                                  a->q_norm_w, a->k_norm_w, a->k_new, a->v_new, a->workspace);
+  if (rc != QIC_SUCCESS) return rc;
+  if (S < 0) return QIC_ERROR_INVALID_VALUE;
   const int G = H / Hkv;
-  if (!supported_head_dim(D) || G > qic::kMaxGroup) return QIC_ERROR_NOT_SUPPORTED;
   const bool paged = a->page_table != nullptr;
   if (paged && (a->page_size <= 0 || a->page_size % 8 != 0)) return QIC_ERROR_NOT_SUPPORTED;
-  const bool fuse_q = (a->flags & QIC_FUSE_Q_PROLOGUE) != 0;
-  const bool fuse_app = (a->flags & QIC_FUSE_APPEND) != 0;
-  if (fuse_q && !a->q_norm_w) return QIC_ERROR_INVALID_VALUE;
-  if (fuse_app && (!a->k_new || !a->v_new || !a->k_norm_w || S < 1)) return QIC_ERROR_INVALID_VALUE;
-  if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned2(a->out) ||
-      (a->gate && !aligned2(a->gate)) || (fuse_q && !aligned16(a->q_norm_w)) ||
-      (fuse_app && (!aligned16(a->k_new) || !aligned16(a->v_new) || !aligned16(a->k_norm_w))) ||
-      (a->workspace && !aligned16(a->workspace)))
-    return QIC_ERROR_MISALIGNED;
+  if ((a->flags & QIC_FUSE_APPEND) && S < 1) return QIC_ERROR_INVALID_VALUE;
   const int kv_dim = Hkv * D;
   const size_t row_bytes = static_cast<size_t>(kv_dim) * 2;
   int64_t cache_tokens = a->cache_tokens;
@@ -224,66 +277,162 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
 
   qic::AttnParams p;
   std::memset(&p, 0, sizeof(p));
-  int box_h = qic::kStageTokens;
-  if (paged) {
-    box_h = a->page_size & (-a->page_size);  // largest power of two dividing P
-    if (box_h > qic::kStageTokens) box_h = qic::kStageTokens;
-  }
+  const int tok = qic::stage_tokens(D);
   int lbh = 0;
-  while ((1 << lbh) < box_h) ++lbh;
-  int rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, cache_tokens, kv_dim, box_h);
+  const int box_h = box_height(paged, a->page_size, tok, &lbh);
+  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, cache_tokens, kv_dim, box_h);
   if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, cache_tokens, kv_dim, box_h);
   if (rc != QIC_SUCCESS) return rc;
 
-  const int n_stages = (S + qic::kStageTokens - 1) / qic::kStageTokens;
-  int n_splits = a->num_splits;
-  if (n_splits <= 0) n_splits = std::max(1, sm_count() / Hkv);
-  n_splits = std::max(1, std::min(std::min(n_splits, n_stages), qic::kMaxSplits));
-  int* status = nullptr;
-  int* counters = nullptr;
-  float* part = nullptr;
-  if (a->workspace == nullptr) {
-    n_splits = 1;
-  } else {
-    const size_t need = qic::kWsHeader + align256(static_cast<size_t>(Hkv) * sizeof(int)) +
-                        static_cast<size_t>(Hkv) * n_splits * qic::partial_floats(G, D) * sizeof(float);
-    if (a->workspace_bytes < need) return QIC_ERROR_WORKSPACE;
-    char* ws = static_cast<char*>(a->workspace);
-    status = reinterpret_cast<int*>(ws);
-    counters = reinterpret_cast<int*>(ws + qic::kWsHeader);
-    part = reinterpret_cast<float*>(ws + qic::kWsHeader + align256(static_cast<size_t>(Hkv) * sizeof(int)));
+  const int n_stages = (S + tok - 1) / tok;
+  int n_splits = a->num_splits, cluster = a->cluster_size;
+  if (cluster < 0 || cluster > qic::kMaxCluster) return QIC_ERROR_INVALID_VALUE;
+  if (n_splits <= 0) {
+    // As many CTAs as can be resident in one wave: clusters of 8 (measured best on B200),
+    // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
+    if (cluster == 0) cluster = 8;
+    int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
+    if (max_clusters <= 0) max_clusters = (2 * sm_count()) / cluster;
+    int nclust = std::max(1, max_clusters / Hkv);
+    n_splits = cluster * nclust;
+    if (n_splits > n_stages) {
+      nclust = std::max(1, n_stages / cluster);
+      if (n_stages < cluster) cluster = n_stages;
+      n_splits = cluster * nclust;
+    }
   }
-
-  p.q = a->q;
-  p.gate = a->gate;
-  p.out = a->out;
-  p.k_cache = a->k_cache;
-  p.v_cache = a->v_cache;
+  if (cluster == 0) cluster = std::min(n_splits, qic::kMaxCluster);
+  while (cluster > 1 && n_splits % cluster != 0) --cluster;
+  if (n_splits > qic::kMaxSplits) return QIC_ERROR_INVALID_VALUE;
+  if (a->workspace == nullptr) {
+    n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
+    cluster = n_splits;
+  }
+  const int n_clusters = n_splits / cluster;
+  if (n_clusters > 1) {
+    const size_t need = qic::kWsPartialOffset +
+                        static_cast<size_t>(Hkv) * n_clusters * qic::partial_floats(G, D) * sizeof(float);
+    if (a->workspace_bytes < need || Hkv * cluster > qic::kMaxCounters) return QIC_ERROR_WORKSPACE;
+  }
+  if (a->workspace != nullptr) {
+    char* ws = static_cast<char*>(a->workspace);
+    p.status = reinterpret_cast<int*>(ws);
+    if (a->workspace_bytes >= qic::kWsPartialOffset) {
+      p.counters = reinterpret_cast<int*>(ws + qic::kWsHeader);
+      p.part = reinterpret_cast<float*>(ws + qic::kWsPartialOffset);
+      p.num_counters = std::min(Hkv * cluster, qic::kMaxCounters);
+      p.part_slots = static_cast<int>(std::min<size_t>(
+          INT32_MAX, (a->workspace_bytes - qic::kWsPartialOffset) / (qic::partial_floats(G, D) * sizeof(float))));
+    }
+  }
+  p.cluster = cluster;
+  fill_common(p, H, Hkv, D, a->q, a->gate, a->out, a->k_cache, a->v_cache, a->flags, a->eps, a->rope_theta,
+              a->q_norm_w, a->k_norm_w, a->k_new, a->v_new);
   p.page_table = a->page_table;
-  p.q_norm_w = a->q_norm_w;
-  p.k_norm_w = a->k_norm_w;
-  p.k_new = a->k_new;
-  p.v_new = a->v_new;
-  p.part = part;
-  p.counters = counters;
-  p.status = status;
   p.cache_tokens = cache_tokens;
-  p.H = H;
-  p.Hkv = Hkv;
-  p.G = G;
-  p.head_dim = D;
   p.seq_len = S;
   p.page_size = paged ? a->page_size : 0;
   p.box_h = box_h;
   p.log2_box_h = lbh;
   p.n_stages = n_stages;
   p.n_splits = n_splits;
-  p.flags = static_cast<int>(a->flags & (QIC_FUSE_Q_PROLOGUE | QIC_FUSE_APPEND));
-  p.eps = a->eps;
-  p.theta = a->rope_theta;
-  p.scale_log2 = static_cast<float>((1.0 / std::sqrt(static_cast<double>(D))) * 1.4426950408889634);
-  p.timeout_ns = timeout_ns();
   return cuda_status(qic::launch_decode_attention(a->dtype, D, p, st));
+}
+
+int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
+                   int target_ctas, void* plan, int max_items, int* items, size_t* workspace_bytes) {
+  if (!seq_lens || batch <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || !items ||
+      !workspace_bytes || max_items < 0 || (max_items > 0 && !plan))
+    return QIC_ERROR_INVALID_VALUE;
+  if (!supported_head_dim(head_dim)) return QIC_ERROR_NOT_SUPPORTED;
+  const int tok = qic::stage_tokens(head_dim);
+  long long total = 0;
+  for (int b = 0; b < batch; ++b) {
+    if (seq_lens[b] < 1) return QIC_ERROR_INVALID_VALUE;
+    total += static_cast<long long>((seq_lens[b] + tok - 1) / tok) * num_kv_heads;
+  }
+  if (target_ctas <= 0) target_ctas = 16 * sm_count();
+  const long long chunk = std::max<long long>(1, (total + target_ctas - 1) / target_ctas);
+  std::vector<qic::WorkItem> out;
+  int part_base = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int n = (seq_lens[b] + tok - 1) / tok;
+    const int ns = static_cast<int>(std::min<long long>(std::min(n, qic::kMaxSplits), (n + chunk - 1) / chunk));
+    for (int h = 0; h < num_kv_heads; ++h) {
+      for (int s = 0; s < ns; ++s) {
+        qic::WorkItem w;
+        w.b = b;
+        w.kvh = h;
+        w.split = s;
+        w.nsplit = ns;
+        w.st_lo = static_cast<int>(static_cast<long long>(s) * n / ns);
+        w.st_hi = static_cast<int>(static_cast<long long>(s + 1) * n / ns);
+        w.seq_len = seq_lens[b];
+        w.part_base = part_base;
+        out.push_back(w);
+      }
+      part_base += ns;
+    }
+  }
+  // longest first, so the last wave is made of the shortest items
+  std::stable_sort(out.begin(), out.end(), [](const qic::WorkItem& x, const qic::WorkItem& y) {
+    return (x.st_hi - x.st_lo) > (y.st_hi - y.st_lo);
+  });
+  const int G = num_heads / num_kv_heads;
+  *items = static_cast<int>(out.size());
+  if (static_cast<long long>(batch) * num_kv_heads > qic::kMaxCounters) return QIC_ERROR_NOT_SUPPORTED;
+  *workspace_bytes = qic::kWsPartialOffset +
+                     static_cast<size_t>(part_base) * qic::partial_floats(G, head_dim) * sizeof(float);
+  if (static_cast<int>(out.size()) > max_items) return max_items == 0 ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
+  std::memcpy(plan, out.data(), out.size() * sizeof(qic::WorkItem));
+  return QIC_SUCCESS;
+}
+
+int qic_batch_decode_attention(const qic_batch_decode_args* a, qic_stream_t stream) {
+  if (a == nullptr) return QIC_ERROR_INVALID_VALUE;
+  const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim;
+  int rc = check_attention_common(a->dtype, H, Hkv, D, a->flags, a->q, a->out, a->k_cache, a->v_cache, a->gate,
+                                  a->q_norm_w, a->k_norm_w, a->k_new, a->v_new, a->workspace);
+  if (rc != QIC_SUCCESS) return rc;
+  if (a->batch <= 0 || !a->block_tables || a->max_pages_per_seq <= 0 || !a->plan || a->plan_items <= 0 ||
+      a->cache_tokens <= 0 || a->cache_tokens > (int64_t(1) << 31) - 1)
+    return QIC_ERROR_INVALID_VALUE;
+  if (a->page_size <= 0 || a->page_size % 8 != 0) return QIC_ERROR_NOT_SUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a->plan) & 15u) != 0) return QIC_ERROR_MISALIGNED;
+  const int G = H / Hkv;
+  if (static_cast<long long>(a->batch) * Hkv > qic::kMaxCounters) return QIC_ERROR_NOT_SUPPORTED;
+  const size_t head = qic::kWsPartialOffset;
+  if (a->workspace == nullptr || a->workspace_bytes < head) return QIC_ERROR_WORKSPACE;
+  const size_t slots = (a->workspace_bytes - head) / (qic::partial_floats(G, D) * sizeof(float));
+  qic::AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int tok = qic::stage_tokens(D);
+  int lbh = 0;
+  const int box_h = box_height(true, a->page_size, tok, &lbh);
+  const int kv_dim = Hkv * D;
+  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, a->cache_tokens, kv_dim, box_h);
+  if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, a->cache_tokens, kv_dim, box_h);
+  if (rc != QIC_SUCCESS) return rc;
+  char* ws = static_cast<char*>(a->workspace);
+  p.status = reinterpret_cast<int*>(ws);
+  p.counters = reinterpret_cast<int*>(ws + qic::kWsHeader);
+  p.part = reinterpret_cast<float*>(ws + head);
+  p.num_counters = a->batch * Hkv;  // <= kMaxCounters
+  p.part_slots = static_cast<int>(std::min<size_t>(slots, INT32_MAX));
+  fill_common(p, H, Hkv, D, a->q, a->gate, a->out, a->k_cache, a->v_cache, a->flags, a->eps, a->rope_theta,
+              a->q_norm_w, a->k_norm_w, a->k_new, a->v_new);
+  p.page_table = a->block_tables;
+  p.table_bstride = a->max_pages_per_seq;
+  p.q_bstride = static_cast<long long>(H) * D;
+  p.kv_new_bstride = static_cast<long long>(Hkv) * D;
+  p.plan = static_cast<const qic::WorkItem*>(a->plan);
+  p.cache_tokens = a->cache_tokens;
+  p.page_size = a->page_size;
+  p.box_h = box_h;
+  p.log2_box_h = lbh;
+  p.n_splits = a->plan_items;  // grid size
+  p.cluster = 1;
+  return cuda_status(qic::launch_decode_attention(a->dtype, D, p, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int qic_gated_delta_decode(const qic_gdn_args* a, qic_stream_t stream) {

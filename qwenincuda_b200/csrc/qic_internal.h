@@ -10,18 +10,35 @@
 
 namespace qic {
 
-constexpr int kStageTokens = 32;     // tokens per TMA pipeline stage
 constexpr int kConsumerWarps = 4;    // warps that run the mma pipeline
-constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kProducerWarps = 2;    // warps issuing TMA copies (K copies / V copies)
+constexpr int kAttnThreads = (kConsumerWarps + kProducerWarps) * 32;
+constexpr int kMaxCluster = 16;      // CTAs of one (sequence, kv head) merged through DSMEM
 constexpr int kMaxGroup = 8;         // query heads per kv head handled by one n8 mma tile
 constexpr int kMaxSplits = 256;      // KV splits per kv head
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s bound on every device wait
 
-// Workspace layout: [status int | pad to 256][counters int[Hkv*batch] | pad to 256][partials]
+// Workspace layout, the same for every shape so one workspace can serve calls of any
+// shape: [status word | pad to 256 B][kMaxCounters merge counters][partial slots].
+// Counters are only ever used as counters and are left at zero by every call.
 constexpr size_t kWsHeader = 256;
+constexpr int kMaxCounters = 8192;
+constexpr size_t kWsPartialOffset = kWsHeader + static_cast<size_t>(kMaxCounters) * sizeof(int);
+
+// Tokens per TMA pipeline stage: one stage is 16 KB of K+V for head_dim 128/256
+// (32 / 16 tokens) and 8 KB for head_dim 64 (32 tokens).
+__host__ __device__ constexpr int stage_tokens(int head_dim) { return head_dim > 128 ? 16 : 32; }
 
 // One partial of a (kv head, split): lse[G] (log2 domain) then o[G][D] (normalised), fp32.
 __host__ __device__ constexpr int partial_floats(int G, int D) { return ((G * (D + 1)) + 3) & ~3; }
+
+// Work of one CTA in a planned (batched) launch: stages [st_lo, st_hi) of sequence b
+// for kv head kvh, being split `split` of `nsplit` for that (b, kvh); its partial goes
+// to slot part_base + split. 32 bytes.
+struct WorkItem {
+  int b, kvh, split, nsplit;
+  int st_lo, st_hi, seq_len, part_base;
+};
 
 struct AttnParams {
   CUtensorMap tm_k;                  // 2D map over [tokens, kv_dim], box {64, box_h}, 128B swizzle
@@ -36,16 +53,23 @@ struct AttnParams {
   const void* k_norm_w;
   const void* k_new;
   const void* v_new;
-  float* part;                       // [Hkv][n_splits][partial_floats]
-  int* counters;                     // [Hkv]
+  float* part;                       // partial slots, partial_floats each
+  int* counters;                     // one merge counter per (sequence, kv head)
   int* status;                       // device status word
+  const WorkItem* plan;              // null: one sequence, grid (n_splits, Hkv)
+  long long q_bstride;               // elements between sequences in q / out / gate
+  long long kv_new_bstride;          // elements between sequences in k_new / v_new
+  int table_bstride;                 // entries between sequences' block-table rows
+  int part_slots;                    // partial slots available in the workspace
+  int num_counters;                  // merge counters available in the workspace
   int64_t cache_tokens;
   int H, Hkv, G;
   int head_dim;                      // runtime copy of D (mirrors the reference's runtime arithmetic)
   int seq_len;
   int page_size;
   int box_h, log2_box_h;
-  int n_stages, n_splits;
+  int n_stages, n_splits;            // n_splits = cluster * n_clusters CTAs per kv head
+  int cluster;                       // CTAs per thread-block cluster along the splits
   int flags;
   float eps, theta, scale_log2;
   uint64_t timeout_ns;
@@ -54,6 +78,8 @@ struct AttnParams {
 // Launchers (attn_kernel.cu)
 cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream);
 size_t decode_attention_smem_bytes(int head_dim);
+// Clusters of `cluster` CTAs of the decode kernel that can be resident at once (0 if unknown).
+int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster);
 
 // Standalone ops (rowops.cu)
 cudaError_t launch_head_rmsnorm(int dtype, const void* x, const void* w, int num_heads, int head_dim, float eps,

@@ -18,6 +18,9 @@ from .abi import (
     QIC_DTYPE_F16,
     QIC_FUSE_APPEND,
     QIC_FUSE_Q_PROLOGUE,
+    QIC_PDL,
+    QIC_PLAN_ITEM_BYTES,
+    BatchDecodeArgs,
     DecodeArgs,
     GdnArgs,
     check,
@@ -100,7 +103,7 @@ def kv_append(k_new, v_new, k_norm_w, eps, rope_theta, position, k_cache, v_cach
 def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, seq_len, page_table=None,
                 page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
                 rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
-                cache_tokens=None) -> DecodeArgs:
+                cache_tokens=None, pdl=False, cluster_size=0) -> DecodeArgs:
     a = DecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads = num_heads
@@ -115,7 +118,7 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
     a.page_table = _ptr(page_table)
     a.gate = _ptr(gate)
     a.out = _ptr(out)
-    a.flags = (QIC_FUSE_Q_PROLOGUE if fuse_q else 0) | (QIC_FUSE_APPEND if fuse_append else 0)
+    a.flags = _flags(fuse_q, fuse_append, pdl)
     a.eps = eps
     a.rope_theta = rope_theta
     a.q_norm_w = _ptr(q_norm_w)
@@ -126,7 +129,12 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
         a.workspace = workspace.ptr
         a.workspace_bytes = workspace.nbytes
     a.num_splits = num_splits
+    a.cluster_size = cluster_size
     return a
+
+
+def _flags(fuse_q, fuse_append, pdl):
+    return (QIC_FUSE_Q_PROLOGUE if fuse_q else 0) | (QIC_FUSE_APPEND if fuse_append else 0) | (QIC_PDL if pdl else 0)
 
 
 def decode_attention(stream=None, **kw):
@@ -165,3 +173,60 @@ def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_sta
     g.conv_w, g.dt_bias, g.a_log, g.norm_w = _ptr(conv_w), _ptr(dt_bias), _ptr(a_log), _ptr(norm_w)
     g.conv_state, g.recurrent_state, g.out = _ptr(conv_state), _ptr(recurrent_state), _ptr(out)
     check(lib().qic_gated_delta_decode(ctypes.byref(g), _stream(stream)), "qic_gated_delta_decode")
+
+
+class BatchPlan:
+    """Work plan of a batched paged decode (qic_batch_plan), with its device copy and
+    the workspace it needs. seq_lens are host integers: tokens attended per sequence."""
+
+    def __init__(self, seq_lens, num_heads, num_kv_heads, head_dim, target_ctas=0, device=None, stream=None):
+        L = lib()
+        lens = (ctypes.c_int32 * len(seq_lens))(*[int(x) for x in seq_lens])
+        items = ctypes.c_int(0)
+        wsb = ctypes.c_size_t(0)
+        check(L.qic_batch_plan(ctypes.cast(lens, ctypes.c_void_p), len(seq_lens), num_heads, num_kv_heads, head_dim,
+                               target_ctas, None, 0, ctypes.byref(items), ctypes.byref(wsb)), "qic_batch_plan")
+        host = torch.empty(items.value * QIC_PLAN_ITEM_BYTES, dtype=torch.uint8)
+        check(L.qic_batch_plan(ctypes.cast(lens, ctypes.c_void_p), len(seq_lens), num_heads, num_kv_heads, head_dim,
+                               target_ctas, host.data_ptr(), items.value, ctypes.byref(items), ctypes.byref(wsb)),
+              "qic_batch_plan")
+        self.items = items.value
+        self.host = host
+        self.device_plan = host.to(device or "cuda")
+        self.workspace_bytes = int(wsb.value)
+        self.workspace = torch.zeros(self.workspace_bytes, dtype=torch.uint8, device=device or "cuda")
+        self.seq_lens = [int(x) for x in seq_lens]
+
+    def status(self, stream=None) -> int:
+        v = ctypes.c_int(0)
+        check(lib().qic_workspace_status(self.workspace.data_ptr(), _stream(stream), ctypes.byref(v)),
+              "qic_workspace_status")
+        return v.value
+
+
+def batch_decode_args(*, plan: BatchPlan, q, k_cache, v_cache, block_tables, out, num_heads, num_kv_heads, head_dim,
+                      page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
+                      rope_theta=1.0e6, fuse_q=False, fuse_append=False, pdl=False, cache_tokens=None):
+    a = BatchDecodeArgs()
+    a.dtype = dtype_code(k_cache)
+    a.num_heads, a.num_kv_heads, a.head_dim = num_heads, num_kv_heads, head_dim
+    a.batch = len(plan.seq_lens)
+    a.page_size = page_size
+    a.cache_tokens = cache_tokens if cache_tokens is not None else k_cache.numel() // (num_kv_heads * head_dim)
+    a.max_pages_per_seq = block_tables.shape[1]
+    a.flags = _flags(fuse_q, fuse_append, pdl)
+    a.q, a.k_cache, a.v_cache = _ptr(q), _ptr(k_cache), _ptr(v_cache)
+    a.block_tables, a.gate, a.out = _ptr(block_tables), _ptr(gate), _ptr(out)
+    a.eps, a.rope_theta = eps, rope_theta
+    a.q_norm_w, a.k_norm_w, a.k_new, a.v_new = _ptr(q_norm_w), _ptr(k_norm_w), _ptr(k_new), _ptr(v_new)
+    a.plan = plan.device_plan.data_ptr()
+    a.plan_items = plan.items
+    a.workspace = plan.workspace.data_ptr()
+    a.workspace_bytes = plan.workspace_bytes
+    return a
+
+
+def batch_decode_attention(stream=None, **kw):
+    """Batched paged decode over a shared page pool; see qic_batch_decode_attention."""
+    a = batch_decode_args(**kw)
+    check(lib().qic_batch_decode_attention(ctypes.byref(a), _stream(stream)), "qic_batch_decode_attention")

@@ -161,3 +161,76 @@ def make_gdn_inputs(cfg: GdnConfig, device="cuda", dtype=torch.bfloat16) -> dict
         recurrent_state=randn(Hv, dk, dv, std=0.02, dt=torch.float32),
         out=torch.zeros(Hv * dv, device=device, dtype=dtype),
     )
+
+
+@dataclass
+class BatchConfig:
+    """Batched paged decode: `batch` sequences with seeded cached lengths in
+    [min_len, max_len], one token appended per sequence (S_b = cached_b + 1), pages of
+    `page_size` tokens drawn from one shuffled pool of about `pool_tokens` tokens."""
+
+    name: str = "qwen3_8b_batch64"
+    batch: int = 64
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    min_len: int = 512
+    max_len: int = 32768
+    page_size: int = 16
+    pool_tokens: int = 1_100_000
+    kv_std: float = 0.5
+    rope_theta: float = 1.0e6
+    eps: float = 1e-6
+    seed: int = 6
+
+    def seq_lens(self) -> list[int]:
+        g = torch.Generator().manual_seed(self.seed)
+        cached = torch.randint(self.min_len, self.max_len + 1, (self.batch,), generator=g)
+        return [int(c) + 1 for c in cached]
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+
+def batched_bytes(seq_lens, kv_dim: int) -> int:
+    """Algorithmic bytes of one batched step: K+V read for every attended token plus the appends."""
+    return sum(2 * s * kv_dim * 2 for s in seq_lens) + len(seq_lens) * 2 * kv_dim * 2
+
+
+def make_batched_inputs(cfg: BatchConfig, *, device="cuda", dtype=torch.bfloat16, seq_lens=None) -> dict:
+    lens = seq_lens if seq_lens is not None else cfg.seq_lens()
+    P = cfg.page_size
+    pages_per = [(s + P - 1) // P for s in lens]
+    need = sum(pages_per)
+    pool_pages = max((cfg.pool_tokens + P - 1) // P, need)
+    gen = torch.Generator().manual_seed(cfg.seed + 1)
+    perm = torch.randperm(pool_pages, generator=gen)
+    max_pages = max(pages_per)
+    tables = torch.zeros(len(lens), max_pages, dtype=torch.int32)
+    at = 0
+    for b, n in enumerate(pages_per):
+        tables[b, :n] = perm[at:at + n].to(torch.int32)
+        at += n
+    g = torch.Generator(device=device)
+    g.manual_seed(cfg.seed)
+    H, Hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+
+    def randn(*shape, std=1.0):
+        return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * std).to(dtype)
+
+    cache_tokens = pool_pages * P
+    B = len(lens)
+    return dict(
+        seq_lens=lens,
+        block_tables=tables.to(device),
+        k_cache=randn(cache_tokens, Hkv, d, std=cfg.kv_std),
+        v_cache=randn(cache_tokens, Hkv, d, std=cfg.kv_std),
+        q=randn(B, H, d),
+        k_new=randn(B, Hkv, d),
+        v_new=randn(B, Hkv, d, std=cfg.kv_std),
+        q_norm_w=torch.ones(d, device=device, dtype=dtype),
+        k_norm_w=torch.ones(d, device=device, dtype=dtype),
+        out=torch.zeros(B, H, d, device=device, dtype=dtype),
+        cache_tokens=cache_tokens,
+    )

@@ -5,7 +5,7 @@ oracle/Makefile into oracle/_ref/) on small seeded inputs on a CUDA device and s
 inputs and outputs as torch files. tests/test_oracle_cpu.py checks the CPU oracle
 against them, which pins the oracle to the reference's behaviour.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [output_dir]
 """
 from __future__ import annotations
 
@@ -20,7 +20,8 @@ sys.path.insert(0, str(HERE.parents[1]))
 from oracle.oracle import RefKernels  # noqa: E402
 
 
-def main() -> None:
+def main(out_dir: Path = HERE) -> None:
+    out_dir.mkdir(parents=True, exist_ok=True)
     g = torch.Generator(device="cuda").manual_seed(2024)
     n = 0
     for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float16, "f16")):
@@ -43,7 +44,7 @@ def main() -> None:
                         out=out.cpu())
             if paged:
                 case["table"] = table.cpu()
-            torch.save(case, HERE / f"attention_{tag}_h{H}_kv{Hkv}_d{d}_s{S}_{'paged' if paged else 'flat'}.pt")
+            torch.save(case, out_dir / f"attention_{tag}_h{H}_kv{Hkv}_d{d}_s{S}_{'paged' if paged else 'flat'}.pt")
             n += 1
         # head RMSNorm
         H, d = 16, 128
@@ -52,7 +53,7 @@ def main() -> None:
         out = torch.empty_like(x)
         ref.head_rmsnorm(x, w, H, d, 1e-6, out)
         torch.save(dict(kind="head_rmsnorm", H=H, d=d, eps=1e-6, x=x.cpu(), w=w.cpu(), out=out.cpu()),
-                   HERE / f"head_rmsnorm_{tag}.pt")
+                   out_dir / f"head_rmsnorm_{tag}.pt")
         n += 1
         # RoPE at small and large positions
         for pos in (0, 3, 1024, 131072):
@@ -60,16 +61,16 @@ def main() -> None:
             out = x.clone()
             ref.rope_inplace(out, 8, 128, pos, 1.0e6)
             torch.save(dict(kind="rope", H=8, d=128, pos=pos, theta=1.0e6, x=x.cpu(), out=out.cpu(),
-                            atol=2.0 ** -7 if pos <= 1024 else 0.05), HERE / f"rope_{tag}_pos{pos}.pt")
+                            atol=2.0 ** -7 if pos <= 1024 else 0.05), out_dir / f"rope_{tag}_pos{pos}.pt")
             n += 1
         x = torch.randn(1024, generator=g, device="cuda").to(dtype)
         gate = torch.randn(1024, generator=g, device="cuda").to(dtype)
         out = x.clone()
         ref.sigmoid_mul_inplace(out, gate, 1024)
-        torch.save(dict(kind="sigmoid_mul", x=x.cpu(), gate=gate.cpu(), out=out.cpu()), HERE / f"sigmoid_mul_{tag}.pt")
+        torch.save(dict(kind="sigmoid_mul", x=x.cpu(), gate=gate.cpu(), out=out.cpu()), out_dir / f"sigmoid_mul_{tag}.pt")
         n += 1
-    print(f"wrote {n} golden cases to {HERE}")
+    print(f"wrote {n} golden cases to {out_dir}")
 
 
 if __name__ == "__main__":
-    main()
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else HERE)

@@ -99,3 +99,15 @@ def test_argument_validation_without_device():
     g.dtype, g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim, g.conv_kernel = 1, 16, 32, 64, 128, 4
     assert L.qic_gated_delta_decode(ctypes.byref(g), None) == 2
     assert L.qic_kv_append(1, None, None, None, 1e-6, 1e6, 0, None, None, None, 16, 10, 8, 128, None) == 1
+
+
+def test_libraries_bind_their_own_symbols():
+    """libqic.so exports the kernels.cuh C++ names and so does the reference's fp16
+    build; both are linked -Bsymbolic so neither library's internal calls can be
+    bound to the other's same-named functions when both are loaded in one process."""
+    from qwenincuda_b200 import lib_path
+
+    libs = [lib_path()] + sorted((ROOT / "oracle" / "_ref").glob("libqicref_*.so"))
+    for p in libs:
+        out = subprocess.run(["readelf", "-d", str(p)], capture_output=True, text=True, check=True).stdout
+        assert "SYMBOLIC" in out, p
