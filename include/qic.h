@@ -148,6 +148,22 @@ int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status);
  * and, with flags, the block src/model.cpp:633-652. */
 int qic_decode_attention(const qic_decode_args* args, qic_stream_t stream);
 
+/* Same computation as qic_decode_attention, for callers that cannot allocate device
+ * memory: code written against the reference's kernels.cuh interface has no workspace
+ * to pass, and a per-token decode loop (or a host that reserves all HBM for its own
+ * page pool) must not call cudaMalloc, which synchronises the device. The split-KV
+ * scratch is a 2 MiB array inside this library (qic_noalloc_scratch_bytes), held by
+ * every GPU that loads it until the process exits; args->workspace and
+ * args->workspace_bytes are ignored. The first call on a device looks up the array's
+ * address (make it before any stream capture). Each call clears the array's status
+ * word and counters; calls that overlap on the GPU share the array and race. Shapes
+ * whose partials do not fit return QIC_ERROR_WORKSPACE. No counterpart in the
+ * reference: its kernels keep no scratch. Allocates nothing. */
+int qic_decode_attention_noalloc(const qic_decode_args* args, qic_stream_t stream);
+
+/* Size in bytes of the array qic_decode_attention_noalloc uses. */
+size_t qic_noalloc_scratch_bytes(void);
+
 /* ------------------------------------------------------------------------- */
 /* Batched paged decode over one shared page pool.                            */
 /* ------------------------------------------------------------------------- */

@@ -166,6 +166,8 @@ SIGNATURES = {
          ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t)],
     ),
     "qic_batch_decode_attention": (ctypes.c_int, [ctypes.POINTER(BatchDecodeArgs), _vp]),
+    "qic_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
+    "qic_noalloc_scratch_bytes": (ctypes.c_size_t, []),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -32,6 +32,7 @@ UNITS = [
     ("gdn_kernel.cu", []),
     ("capi.cpp", []),
     ("compat.cu", ["--use_fast_math"]),
+    ("noalloc.cu", []),
 ]
 
 

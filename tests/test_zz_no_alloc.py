@@ -1,0 +1,57 @@
+"""GPU: qic_decode_attention_noalloc, the entry point for callers that cannot allocate
+device memory (code written against the reference's kernels.cuh interface has no
+workspace to pass, and a per-token decode loop must not stop for a synchronising
+cudaMalloc). Its scratch is a fixed array inside the library; this checks, through
+the C-ABI, that two calls in a row give the same results as qic_decode_attention
+with a caller-allocated workspace. Collected last so a failure here comes after
+every other test has run; it also passes alone in a fresh process."""
+import ctypes
+
+import pytest
+import torch
+
+import qwenincuda_b200 as q
+from conftest import allclose_report
+from qwenincuda_b200.workloads import AttnConfig, make_attention_inputs
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _args(inp, layer, out, cfg, workspace=None):
+    return q.ops.decode_args(
+        q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=out, num_heads=cfg.num_heads,
+        num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len, page_table=inp.page_table[layer],
+        page_size=cfg.page_size, workspace=workspace, cache_tokens=inp.cache_tokens)
+
+
+def test_noalloc_two_calls_match_workspace_entry_point():
+    L = q.lib()
+    assert L.qic_noalloc_scratch_bytes() == 2 << 20
+    # long enough that several thread-block clusters merge through the scratch partials
+    cfg = AttnConfig("noalloc", 32, 8, 128, 12000, layers=2, seed=21)
+    inp = make_attention_inputs(cfg, paged=True)
+    ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
+    stream = torch.cuda.current_stream().cuda_stream
+    for layer in range(2):
+        want = torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+        a = _args(inp, layer, want, cfg, workspace=ws)
+        assert L.qic_decode_attention(ctypes.byref(a), stream) == 0
+        got = torch.full_like(want, float("nan"))
+        b = _args(inp, layer, got, cfg)
+        assert L.qic_decode_attention_noalloc(ctypes.byref(b), stream) == 0
+        torch.cuda.synchronize()
+        assert ws.status() == 0
+        ok, err, idx = allclose_report(got, want, ATOL, RTOL)
+        assert ok, f"call {layer}: max abs err {err} at {idx}"
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    """A split count whose partials exceed the fixed array is refused before launch."""
+    L = q.lib()
+    cfg = AttnConfig("noalloc_big", 64, 8, 256, 40000, seed=22)
+    inp = make_attention_inputs(cfg, paged=True)
+    out = torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+    a = _args(inp, 0, out, cfg)
+    a.num_splits, a.cluster_size = 256, 1  # 8 kv heads x 256 partial slots of 8 KB each
+    assert L.qic_decode_attention_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == 4
