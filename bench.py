@@ -1,24 +1,32 @@
 """Benchmark of the decode-time KV-cache hot path (one JSON line on rank 0).
 
-Workload (default): Qwen3-8B full-attention decode, 36 layers, 32 query heads,
-8 kv heads, head_dim 128, bf16, 8191 cached tokens + 1 appended per layer
-(S = 8192), paged layout (page 16, seeded shuffled block table per layer). One step
-= for every layer, one fused call: q head-RMSNorm + RoPE, k head-RMSNorm + RoPE +
-page write of the new token (append), split-KV attention over all 8192 positions.
-Synthetic seeded data; the step's inputs (1.2 GB of K/V) are larger than L2.
+Default workload (the benchmark configuration the metric is quoted on): Qwen3-8B
+full-attention decode, 36 layers, 32 query heads, 8 kv heads, head_dim 128, bf16,
+8191 cached tokens + 1 appended per layer (S = 8192), paged layout (page 16, seeded
+shuffled block table per layer). One step = for every layer, one fused launch: q
+head-RMSNorm + RoPE, k head-RMSNorm + RoPE + page write of the new token (append),
+split-KV attention over all 8192 positions; layers chained with programmatic
+dependent launch inside a CUDA graph. Synthetic seeded data; the step's K/V (1.2 GB)
+is larger than L2. The contiguous (flash) layout is timed as well.
 
 metric: decode-attn KV-read GB/s = (K+V bytes read for S tokens + append bytes) per
-layer x layers / step time; also reported as us per layer. N > 1 GPUs run
-independent replicas (one process per GPU, no collective on this path).
+layer x layers / step time; also reported as us per layer. N > 1 GPUs run one
+independent replica per GPU (this path has no collective): value = total bytes / the
+slowest rank's step time.
 
-`--impl reference` (rank 0 only): the reference's algorithm on the host cores — the
-oracle's C restatement of src/kernels.cu's paged attention with OpenMP over heads —
-as the line's value, plus the reference's own kernels built for sm_100a timed on
-the GPU for the same layers.
+Other workloads (--workload): qwen3_0p6b_s1025, qwen35_gated_s32769 (d=256 with the
+output gate), qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step;
+state bytes), qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64
+(64 sequences, lengths 512..32768, one shared page pool, one batched launch).
+
+--impl reference (rank 0 only): the reference's attention on the host cores — the
+oracle's C restatement of src/kernels.cu's paged attention, OpenMP over heads — as the
+line's value, plus the reference's own kernels built for sm_100a timed on the GPU.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -33,6 +41,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+ATTN_WORKLOADS = ("qwen3_0p6b_s1025", "qwen3_8b_s8192", "qwen35_gated_s32769", "qwen3_8b_s131073")
 
 
 def load_peaks():
@@ -43,10 +52,26 @@ def load_peaks():
     return dict(PEAKS_FALLBACK, source="fallback")
 
 
+def measured_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary of
+    this workload (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch: N')."""
+    for p in (ROOT / "profiles").glob(f"*_{workload}.md"):
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons with NVML while the timed region runs."""
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    NAMES = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+             0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.period = period_s
         self.samples: list[int] = []
         self.reasons: set[str] = set()
@@ -65,15 +90,11 @@ class ClockSampler:
 
     def _run(self):
         n = self.nvml
-        names = {
-            0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
-            0x80: "hw_power_brake_slowdown",
-        }
         while not self._stop.is_set():
             try:
                 self.samples.append(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
                 mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                for bit, name in names.items():
+                for bit, name in self.NAMES.items():
                     if mask & bit:
                         self.reasons.add(name)
             except Exception:
@@ -92,15 +113,11 @@ class ClockSampler:
             self._thread.join()
 
     def summary(self):
-        return {
-            "sm_mhz": statistics.median(self.samples) if self.samples else None,
-            "sm_max_mhz": self.max_mhz,
-            "reasons": sorted(self.reasons),
-            "samples": len(self.samples),
-        }
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def dist_setup(gpus: int):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -110,7 +127,8 @@ def dist_setup(gpus: int):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return world, rank, local
@@ -133,43 +151,13 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def layer_bytes(cfg) -> int:
-    return cfg.kv_read_bytes() + cfg.append_bytes()
-
-
-def build_step(inp, ws, pdl=True):
-    """Returns a callable issuing one decode step (all layers) through the public API."""
-    import qwenincuda_b200 as q
-
-    cfg = inp.cfg
-    args = []
-    for layer in range(inp.q.shape[0]):
-        args.append(q.ops.decode_args(
-            q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=inp.out[layer],
-            num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
-            page_table=inp.page_table[layer] if inp.paged else None, page_size=cfg.page_size,
-            gate=None if inp.gate is None else inp.gate[layer], q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w,
-            k_new=inp.k_new[layer], v_new=inp.v_new[layer], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True,
-            fuse_append=True, workspace=ws, cache_tokens=inp.cache_tokens, pdl=pdl))
-    L = q.lib()
-    import ctypes
-
-    def step():
-        s = torch.cuda.current_stream().cuda_stream
-        for a in args:
-            rc = L.qic_decode_attention(ctypes.byref(a), s)
-            if rc != 0:
-                raise q.QicError(rc, "qic_decode_attention")
-
-    return step
-
-
 def capture(fn):
+    """CUDA graph of fn (after one eager run that performs per-device set-up)."""
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        fn()  # warm the per-device attribute set-up outside capture
+        fn()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     with torch.cuda.graph(g):
@@ -178,25 +166,193 @@ def capture(fn):
     return g
 
 
-def time_graph(g, steps, warmup, world):
+def time_graph(g, steps, warmup, world, sampler=None):
+    """ms per replay: W untimed replays, then exactly `steps` replays between CUDA
+    events, bracketed by barrier + synchronize; max over ranks."""
     for _ in range(warmup):
         g.replay()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler is not None:
+        sampler.__enter__()
     start.record()
     for _ in range(steps):
         g.replay()
     end.record()
     torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.__exit__()
     barrier(world)
     return max_over_ranks(start.elapsed_time(end) / steps, world)
 
 
+def _call(fn, args_struct):
+    def run():
+        rc = fn(ctypes.byref(args_struct), torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            import qwenincuda_b200 as q
+
+            raise q.QicError(rc, fn.__name__)
+
+    return run
+
+
+# ---------------------------------------------------------------------------
+# workloads: each returns dict(step=callable, bytes=int, launches=int per step,
+# e2e=(callable, h2d, d2h), kernel=name, status=callable, config=dict)
+# ---------------------------------------------------------------------------
+def attention_workload(name, layout, layers=None):
+    import qwenincuda_b200 as q
+    from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
+
+    cfg = CONFIGS[name]
+    inp = make_attention_inputs(cfg, paged=(layout == "paged"), layers=layers)
+    L_ = inp.q.shape[0]
+    ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
+    fns = []
+    for layer in range(L_):
+        a = q.ops.decode_args(
+            q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=inp.out[layer],
+            num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
+            page_table=inp.page_table[layer] if inp.paged else None, page_size=cfg.page_size,
+            gate=None if inp.gate is None else inp.gate[layer], q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w,
+            k_new=inp.k_new[layer], v_new=inp.v_new[layer], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True,
+            fuse_append=True, workspace=ws, cache_tokens=inp.cache_tokens, pdl=True)
+        fns.append(_call(q.lib().qic_decode_attention, a))
+
+    def step():
+        for f in fns:
+            f()
+
+    hq = inp.q.cpu().pin_memory()
+    hk = inp.k_new.cpu().pin_memory()
+    hv = inp.v_new.cpu().pin_memory()
+    ho = torch.empty_like(inp.out, device="cpu").pin_memory()
+
+    def e2e():
+        inp.q.copy_(hq, non_blocking=True)
+        inp.k_new.copy_(hk, non_blocking=True)
+        inp.v_new.copy_(hv, non_blocking=True)
+        step()
+        ho.copy_(inp.out, non_blocking=True)
+
+    per_layer = cfg.kv_read_bytes() + cfg.append_bytes()
+    return dict(step=step, bytes=per_layer * L_, launches=L_, bytes_per_launch=per_layer,
+                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2), kernel="decode_attn_kernel",
+                status=ws.status, keep=(inp, ws),
+                config={"layout": layout, "page_size": cfg.page_size, "layers": L_, "seq_len": cfg.seq_len,
+                        "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+                        "gate": cfg.gate})
+
+
+def gdn_workload():
+    import qwenincuda_b200 as q
+    from qwenincuda_b200.workloads import GdnConfig, make_gdn_inputs
+
+    cfg = GdnConfig()
+    t = make_gdn_inputs(cfg)
+    g = q.GdnArgs()
+    g.dtype = 1
+    g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
+    g.conv_kernel, g.eps = cfg.conv_kernel, cfg.eps
+    for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state", "out"):
+        setattr(g, k, t[k].data_ptr())
+    step = _call(q.lib().qic_gated_delta_decode, g)
+    hin = {k: t[k].cpu().pin_memory() for k in ("qkv", "z", "b", "a")}
+    hout = torch.empty_like(t["out"], device="cpu").pin_memory()
+
+    def e2e():
+        for k, v in hin.items():
+            t[k].copy_(v, non_blocking=True)
+        step()
+        hout.copy_(t["out"], non_blocking=True)
+
+    h2d = sum(v.numel() * 2 for v in hin.values())
+    return dict(step=step, bytes=cfg.state_bytes(), launches=1, bytes_per_launch=cfg.state_bytes(),
+                e2e=(e2e, h2d, hout.numel() * 2), kernel="gated_delta_kernel", status=lambda: 0, keep=(t, g),
+                config={"num_k_heads": cfg.num_k_heads, "num_v_heads": cfg.num_v_heads, "k_head_dim": 128,
+                        "v_head_dim": 128, "conv_dim": cfg.conv_dim, "conv_kernel": cfg.conv_kernel,
+                        "state": "fp32, resident on the device"})
+
+
+def pair_workload():
+    gdn = gdn_workload()
+    att = attention_workload("qwen35_gated_s32769", "paged")
+
+    def step():
+        gdn["step"]()
+        att["step"]()
+
+    def e2e():
+        gdn["e2e"][0]()
+        att["e2e"][0]()
+
+    return dict(step=step, bytes=gdn["bytes"] + att["bytes"], launches=2, bytes_per_launch=att["bytes_per_launch"],
+                e2e=(e2e, gdn["e2e"][1] + att["e2e"][1], gdn["e2e"][2] + att["e2e"][2]), kernel="decode_attn_kernel",
+                status=att["status"], keep=(gdn, att),
+                config={"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)",
+                        "gdn_bytes": gdn["bytes"], "attention_bytes": att["bytes"]})
+
+
+def batched_workload(world, rank):
+    import qwenincuda_b200 as q
+    from qwenincuda_b200.workloads import BatchConfig, batched_bytes, make_batched_inputs
+
+    cfg = BatchConfig()
+    lens = cfg.seq_lens()
+    inp = make_batched_inputs(cfg, seq_lens=lens)
+    plan = q.BatchPlan(lens, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
+    a = q.ops.batch_decode_args(plan=plan, q=inp["q"], k_cache=inp["k_cache"], v_cache=inp["v_cache"],
+                                block_tables=inp["block_tables"], out=inp["out"], num_heads=cfg.num_heads,
+                                num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, page_size=cfg.page_size,
+                                q_norm_w=inp["q_norm_w"], k_norm_w=inp["k_norm_w"], k_new=inp["k_new"],
+                                v_new=inp["v_new"], fuse_q=True, fuse_append=True, cache_tokens=inp["cache_tokens"])
+    step = _call(q.lib().qic_batch_decode_attention, a)
+    hq = inp["q"].cpu().pin_memory()
+    hk = inp["k_new"].cpu().pin_memory()
+    hv = inp["v_new"].cpu().pin_memory()
+    ho = torch.empty_like(inp["out"], device="cpu").pin_memory()
+
+    def e2e():
+        inp["q"].copy_(hq, non_blocking=True)
+        inp["k_new"].copy_(hk, non_blocking=True)
+        inp["v_new"].copy_(hv, non_blocking=True)
+        step()
+        ho.copy_(inp["out"], non_blocking=True)
+
+    nbytes = batched_bytes(lens, cfg.kv_dim)
+    return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes,
+                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2), kernel="decode_attn_kernel",
+                status=plan.status, keep=(inp, plan, a),
+                config={"batch": cfg.batch, "seq_lens": f"U[{cfg.min_len},{cfg.max_len}]+1, seed {cfg.seed}",
+                        "tokens": sum(lens), "page_size": cfg.page_size, "pool_tokens": inp["cache_tokens"],
+                        "plan_items": plan.items, "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads,
+                        "head_dim": cfg.head_dim})
+
+
+def measure(wl, args, world, local):
+    g = capture(wl["step"])
+    sampler = ClockSampler(local)
+    ms = time_graph(g, args.steps, args.warmup, world, sampler)
+    status = wl["status"]()
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the timed steps")
+    del g
+    ge = capture(wl["e2e"][0])
+    ms_e2e = time_graph(ge, args.steps, args.warmup, world)
+    del ge
+    torch.cuda.synchronize()
+    return ms, ms_e2e, sampler.summary()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline and the reference arm
+# ---------------------------------------------------------------------------
 def cpu_baseline(cfg, budget_s=6.0):
-    """The oracle (C restatement of the reference's paged attention, OpenMP) on a
-    bounded sample of the workload's layers on this host."""
+    """The oracle (C restatement of the reference's paged attention, OpenMP over
+    heads) on a bounded sample of the workload's layers on this host."""
     from oracle.oracle import Oracle
     from qwenincuda_b200.workloads import make_attention_inputs
 
@@ -209,26 +365,25 @@ def cpu_baseline(cfg, budget_s=6.0):
     layers = 0
     t0 = time.perf_counter()
     while True:
-        orc.attention(inp.q[0].flatten(), kc, vc, H, Hkv, d, S, page_table=inp.page_table[0], page_size=cfg.page_size)
+        orc.attention(inp.q[0].flatten(), kc, vc, H, Hkv, d, S, page_table=inp.page_table[0],
+                      page_size=cfg.page_size)
         layers += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
     per_layer = el / layers
-    return {
-        "value": round(layer_bytes(cfg) / per_layer / 1e9, 3),
-        "unit": "GB/s",
-        "us_per_layer": round(per_layer * 1e6, 1),
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{layers} layers of paged attention at S={S} (H={H}, Hkv={Hkv}, d={d}) in {el:.1f} s",
-    }
+    lb = cfg.kv_read_bytes() + cfg.append_bytes()
+    return {"value": round(lb / per_layer / 1e9, 3), "unit": "GB/s", "us_per_layer": round(per_layer * 1e6, 1),
+            "cores": threads, "kind": "port",
+            "sample": f"{layers} layers of paged attention at S={S} (H={H}, Hkv={Hkv}, d={d}) in {el:.1f} s"}
 
 
 def reference_gpu(cfg, layers, steps, warmup):
     """The reference's own kernels (src/kernels.cu built for sm_100a with
-    --use_fast_math) driving the same per-layer sequence as src/model.cpp:633-650."""
-    from oracle.oracle import RefKernels
+    --use_fast_math, bf16 instance) driving the per-layer sequence of
+    src/model.cpp:633-650: head-norm q and k, RoPE q and k, two row copies, paged
+    attention."""
+    from oracle.oracle import RefKernels, _p
     from qwenincuda_b200.workloads import make_attention_inputs
 
     dtype = torch.bfloat16
@@ -236,8 +391,6 @@ def reference_gpu(cfg, layers, steps, warmup):
     inp = make_attention_inputs(cfg, paged=True, layers=layers)
     H, Hkv, d, S, P, pos = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len, cfg.page_size, cfg.position
     lib = ref.lib
-    from oracle.oracle import _p
-
     qbuf = torch.empty(H * d, device="cuda", dtype=dtype)
     kbuf = torch.empty(Hkv * d, device="cuda", dtype=dtype)
     slots = [int(inp.page_table[i][pos // P]) * P + pos % P for i in range(layers)]
@@ -266,15 +419,11 @@ def reference_gpu(cfg, layers, steps, warmup):
         step()
     e.record()
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
-    per_layer_us = ms * 1000 / layers
-    return {
-        "value": round(layer_bytes(cfg) / (per_layer_us * 1e-6) / 1e9, 3),
-        "unit": "GB/s",
-        "us_per_layer": round(per_layer_us, 1),
-        "layers_timed": layers,
-        "build": "src/kernels.cu unmodified, nvcc -gencode arch=compute_100a,code=sm_100a --use_fast_math, bf16 instance",
-    }
+    per_layer_us = s.elapsed_time(e) / steps * 1000 / layers
+    lb = cfg.kv_read_bytes() + cfg.append_bytes()
+    return {"value": round(lb / (per_layer_us * 1e-6) / 1e9, 3), "unit": "GB/s", "us_per_layer": round(per_layer_us, 1),
+            "layers_timed": layers,
+            "build": "src/kernels.cu unmodified, nvcc -gencode arch=compute_100a,code=sm_100a --use_fast_math, bf16"}
 
 
 def run_reference_arm(args, world, rank):
@@ -282,32 +431,23 @@ def run_reference_arm(args, world, rank):
 
     if rank != 0:
         return
-    cfg = CONFIGS[args.workload]
+    name = args.workload if args.workload in ATTN_WORKLOADS else "qwen3_8b_s8192"
+    cfg = CONFIGS[name]
     cb = cpu_baseline(cfg, budget_s=max(2.0, min(20.0, 0.5 * args.steps)))
     line = {
-        "impl": "reference",
-        "metric": "decode-attn KV-read GB/s",
-        "value": cb["value"],
-        "unit": "GB/s",
-        "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(cb["us_per_layer"] * cfg.layers / 1000, 3),
-        "us_per_layer": cb["us_per_layer"],
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": args.workload, "layout": "paged", "layers": cfg.layers, "seq_len": cfg.seq_len,
+        "impl": "reference", "metric": "decode-attn KV-read GB/s", "value": cb["value"], "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(cb["us_per_layer"] * cfg.layers / 1000, 3), "us_per_layer": cb["us_per_layer"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": name, "layout": "paged", "layers": cfg.layers, "seq_len": cfg.seq_len,
                    "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     try:
-        line["reference_kernels_sm100a"] = reference_gpu(cfg, layers=min(4, cfg.layers), steps=max(1, args.steps // 10),
-                                                         warmup=1)
-    except Exception as exc:  # the GPU comparator is extra information only
+        line["reference_kernels_sm100a"] = reference_gpu(cfg, layers=min(2, cfg.layers),
+                                                         steps=max(1, min(5, args.steps // 20)), warmup=1)
+    except Exception as exc:  # extra information only
         line["reference_kernels_sm100a"] = {"unavailable": str(exc)[:200]}
     print(json.dumps(line), flush=True)
 
@@ -319,101 +459,70 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qwen3_8b_s8192")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference_arm(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
         return
 
-    import qwenincuda_b200 as q
-    from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
-
-    cfg = CONFIGS[args.workload]
     peaks = load_peaks()
-    results = {}
-    for layout in ("paged", "contiguous"):
-        inp = make_attention_inputs(cfg, paged=(layout == "paged"))
-        ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
-        step = build_step(inp, ws)
-        g = capture(step)
-        sampler = ClockSampler(local)
-        with sampler:
-            ms = time_graph(g, args.steps, args.warmup, world)
-        status = ws.status()
-        if status != 0:
-            raise RuntimeError(f"device status {status} after timed steps ({layout})")
-        results[layout] = dict(ms=ms, clocks=sampler.summary(), inp=inp, ws=ws, graph=g)
-        if layout == "paged":
-            # e2e: pinned host inputs -> device, the same public-API step, outputs -> pinned host
-            hq = torch.empty_like(inp.q, device="cpu").pin_memory()
-            hk = torch.empty_like(inp.k_new, device="cpu").pin_memory()
-            hv = torch.empty_like(inp.v_new, device="cpu").pin_memory()
-            hq.copy_(inp.q)
-            hk.copy_(inp.k_new)
-            hv.copy_(inp.v_new)
-            ho = torch.empty_like(inp.out, device="cpu").pin_memory()
+    extra = {}
+    if args.workload in ATTN_WORKLOADS:
+        wl = attention_workload(args.workload, "paged", args.layers)
+        ms, ms_e2e, clocks = measure(wl, args, world, local)
+        wl_c = attention_workload(args.workload, "contiguous", args.layers)
+        ms_c, _, _ = measure(wl_c, args, world, local)
+        extra["contiguous"] = {"value": round(world * wl_c["bytes"] / (ms_c * 1e-3) / 1e9, 2), "unit": "GB/s",
+                               "us_per_layer": round(ms_c / wl_c["launches"] * 1000, 3)}
+        del wl_c
+    elif args.workload == "qwen35_gdn":
+        wl = gdn_workload()
+        ms, ms_e2e, clocks = measure(wl, args, world, local)
+    elif args.workload == "qwen35_pair":
+        wl = pair_workload()
+        ms, ms_e2e, clocks = measure(wl, args, world, local)
+    elif args.workload == "qwen3_8b_batch64":
+        wl = batched_workload(world, rank)
+        ms, ms_e2e, clocks = measure(wl, args, world, local)
+    else:
+        raise SystemExit(f"unknown workload {args.workload}")
 
-            def e2e_step():
-                inp.q.copy_(hq, non_blocking=True)
-                inp.k_new.copy_(hk, non_blocking=True)
-                inp.v_new.copy_(hv, non_blocking=True)
-                step()
-                ho.copy_(inp.out, non_blocking=True)
-
-            ge = capture(e2e_step)
-            ms_e2e = time_graph(ge, args.steps, args.warmup, world)
-            results["e2e"] = dict(ms=ms_e2e, h2d=hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2,
-                                  d2h=ho.numel() * 2)
-            del ge
-        del g
-        torch.cuda.synchronize()
-
-    lb = layer_bytes(cfg)
-    step_bytes = lb * cfg.layers
-    paged = results["paged"]
-    value = world * step_bytes / (paged["ms"] * 1e-3) / 1e9
-    per_launch_ms = paged["ms"] / cfg.layers
-    achieved = lb / (per_launch_ms * 1e-3) / 1e9
-    contiguous = results["contiguous"]
+    step_bytes = wl["bytes"]
+    value = world * step_bytes / (ms * 1e-3) / 1e9
+    per_launch_ms = ms / wl["launches"]
+    achieved = wl["bytes_per_launch"] / (per_launch_ms * 1e-3) / 1e9
+    traffic = measured_traffic(args.workload)
     line = {
-        "metric": "decode-attn KV-read GB/s",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(paged["ms"], 4),
-        "us_per_layer": round(per_launch_ms * 1000, 3),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic",
-        "config": {
-            "workload": args.workload, "layout": "paged", "page_size": cfg.page_size, "layers": cfg.layers,
-            "seq_len": cfg.seq_len, "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads,
-            "head_dim": cfg.head_dim, "parallelism": f"replicas{world}" if world > 1 else "single",
-            "step": "per layer: one fused launch (q norm+RoPE, k norm+RoPE+page append, split-KV attention, "
-                    "cluster merge); layers chained with programmatic dependent launch in a CUDA graph",
-            "l2": "step inputs 1.2 GB > 126 MB L2",
-        },
-        "contiguous": {"value": round(world * step_bytes / (contiguous["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
-                       "us_per_layer": round(contiguous["ms"] / cfg.layers * 1000, 3)},
-        "e2e": {"value": round(world * step_bytes / (results["e2e"]["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": results["e2e"]["h2d"], "d2h_bytes_per_step": results["e2e"]["d2h"],
-                "ms_per_step": round(results["e2e"]["ms"], 4)},
-        "roofline": {
-            "bound": "hbm", "kernel": "decode_attn_kernel", "achieved": round(achieved, 1),
-            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "peak_source": peaks["source"], "frac_of_8tbs": round(achieved / 8000.0, 4),
-            "bytes_per_launch": lb, "traffic": None,
-        },
-        "gpu_launches": cfg.layers * args.steps,
-        "clocks": paged["clocks"],
+        "metric": "decode-attn KV-read GB/s" if args.workload != "qwen35_gdn" else "GatedDeltaNet state GB/s",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "us_per_layer": round(per_launch_ms * 1000, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": dict(workload=args.workload, parallelism=f"replicas{world}" if world > 1 else "single",
+                       l2="step inputs larger than the 126 MB L2" if step_bytes > (126 << 20)
+                       else "step smaller than L2; consecutive steps re-read it",
+                       **wl["config"]),
+        **extra,
+        "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2],
+                "ms_per_step": round(ms_e2e, 4)},
+        "roofline": {"bound": "hbm", "kernel": wl["kernel"], "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"],
+                     "launch_time": "step time / launches per step (includes launch gaps)",
+                     "traffic": traffic},
+        "gpu_launches": wl["launches"] * args.steps,
+        "clocks": clocks,
     }
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline and args.workload in ATTN_WORKLOADS:
+        from qwenincuda_b200.workloads import CONFIGS
+
+        line["cpu_baseline"] = cpu_baseline(CONFIGS[args.workload])
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
