@@ -183,7 +183,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
     if (lane == 0) tma_prefetch_desc(pw == 0 ? &p.tm_k : &p.tm_v);
     const CUtensorMap* tmap = pw == 0 ? &p.tm_k : &p.tm_v;
     const int bh = p.box_h;
-    const int box_row_bytes = bh * 128;  // one 64-element chunk of bh token rows
     const int box_bytes = bh * D * 2;    // all chunks of bh token rows
     const int P = p.page_size;
     const int npages = table != nullptr ? (S + P - 1) / P : 0;
@@ -195,9 +194,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
       cur = e0 < npages ? __ldg(table + e0) : 0;
       nxt = e1 < npages ? __ldg(table + e1) : 0;
     }
-    // lane -> (box, chunk) of this warp's copies of a stage
-    const int op_box = lane / Sh::kChunks;
-    const int op_chunk = lane % Sh::kChunks;
+    // lane l copies box l of a stage: every 64-element chunk of bh token rows
+    const int op_box = lane;
     const int kv_off = pw * Sh::kKBytes;
     int issued = 0;
     bool ok = true;
@@ -224,7 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
         }
       }
       const int nbox = (nvalid + bh - 1) / bh;
-      const int nops = nbox * Sh::kChunks;  // copies of this warp
+      const int nops = nbox;  // copies of this warp
       const int jb = min(op_box, nbox - 1);
       const int tb = t0 + jb * bh;
       int row = tb;
@@ -253,8 +251,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
       if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * box_bytes));
       __syncwarp();
       if (lane < nops) {
-        uint8_t* dst = sk + kv_off + op_box * box_bytes + op_chunk * box_row_bytes;
-        tma_load_2d(dst, tmap, &full[slot], kvh * D + op_chunk * 64, row, pol);
+        uint8_t* dst = sk + kv_off + op_box * box_bytes;
+        tma_load_3d(dst, tmap, &full[slot], 0, row, kvh * Sh::kChunks, pol);
       }
       issued = i + 1;
       __syncwarp();

@@ -87,15 +87,21 @@ size_t bytes_to_allocation_end(const void* p) {
   return end > at ? static_cast<size_t>(end - at) : 0;
 }
 
-int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens, int kv_dim, int box_h) {
+// K/V cache view for TMA: a 3D tensor {64 elements, tokens, kv_dim/64 chunks} whose
+// chunk dimension has a 128-byte stride, so one box {64, box_h, head_dim/64} copies
+// every 64-element chunk of one head for box_h token rows. Shared memory receives the
+// box chunk-major ([chunk][token][128 B], 128-byte swizzle), the layout the consumer
+// warps index.
+int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens, int kv_dim, int head_dim,
+                  int box_h) {
   load_driver_entry_points();
   if (g_encode == nullptr) return QIC_ERROR_CUDA;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kv_dim), static_cast<cuuint64_t>(tokens)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kv_dim) * 2};
-  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_h)};
-  cuuint32_t estr[2] = {1u, 1u};
+  cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(kv_dim / 64)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kv_dim) * 2, 128u};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_h), static_cast<cuuint32_t>(head_dim / 64)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = g_encode(map, dtype == QIC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
@@ -280,8 +286,8 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   const int tok = qic::stage_tokens(D);
   int lbh = 0;
   const int box_h = box_height(paged, a->page_size, tok, &lbh);
-  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, cache_tokens, kv_dim, box_h);
-  if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, cache_tokens, kv_dim, box_h);
+  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, cache_tokens, kv_dim, a->head_dim, box_h);
+  if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, cache_tokens, kv_dim, a->head_dim, box_h);
   if (rc != QIC_SUCCESS) return rc;
 
   const int n_stages = (S + tok - 1) / tok;
@@ -410,8 +416,8 @@ int qic_batch_decode_attention(const qic_batch_decode_args* a, qic_stream_t stre
   int lbh = 0;
   const int box_h = box_height(true, a->page_size, tok, &lbh);
   const int kv_dim = Hkv * D;
-  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, a->cache_tokens, kv_dim, box_h);
-  if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, a->cache_tokens, kv_dim, box_h);
+  rc = encode_kv_map(&p.tm_k, a->dtype, a->k_cache, a->cache_tokens, kv_dim, a->head_dim, box_h);
+  if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, a->cache_tokens, kv_dim, a->head_dim, box_h);
   if (rc != QIC_SUCCESS) return rc;
   char* ws = static_cast<char*>(a->workspace);
   p.status = reinterpret_cast<int*>(ws);
