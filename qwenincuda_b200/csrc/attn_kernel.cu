@@ -8,22 +8,25 @@
 //    stages (32 tokens, 16 at head_dim 256), and serves every query head of the GQA
 //    group, so each K/V byte is read from HBM once. Single-sequence launches use a
 //    (splits, kv heads) grid; batched launches read one WorkItem per CTA.
-//  * Two producer warps (one issues the K copies, one the V copies) stream stages
-//    into a 4-stage (64 KB) shared-memory ring with 2D TMA tile loads (box = 64
-//    elements x box_h tokens, 128-byte swizzle, evict-first L2 policy), one copy per
-//    lane. Measured on B200, TMA issue throughput is capped per issuing warp (~24
-//    GB/s with 16-token boxes, independent of ring depth), so a CTA uses two issuing
-//    warps and two CTAs fit per SM. Paged layouts are gathered with one box per page
-//    segment at row page_table[t/P]*P + t%P; two 32-entry windows of the table are
-//    kept in registers and refilled one window ahead.
-//  * Four consumer warps own fixed ring slots (ring depth is a multiple of four, so
-//    a slot is always waited on by the same warp and mbarrier parities cannot
-//    alias). Scores are S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query-head
-//    columns); the online softmax runs in the exp2 domain on the fragments; P^T is
-//    turned into the B operand with movmatrix; O^T += V^T P accumulates in registers.
+//  * Four warps; warp w consumes stages w, w+4, ... of a 4-stage (64 KB) shared-memory
+//    ring (8 stages at head_dim 64) and issues each slot's next copy itself as soon as
+//    it has finished with the slot: 3D TMA tile loads, one box = every 64-element
+//    chunk of bh token rows (128-byte swizzle, evict-first L2 policy), K boxes from
+//    lanes 0-15 and V boxes from lanes 16-31. A stage-level %globaltimer trace showed
+//    separate producer warps to be the limit: a producer's wake-up, page lookup and
+//    issue cost 0.5-0.8 us per stage, so each slot sat idle 2-2.5 us per lap. Three
+//    CTAs fit per SM (registers and shared memory), 12 issuing warps per SM. Paged
+//    layouts are gathered with one box per page segment at row
+//    page_table[t/P]*P + t%P; each warp loads the table entries of its next stage
+//    one stage ahead.
+//  * Slots are owned by one warp (ring depth is a multiple of four), so mbarrier
+//    parities cannot alias. Scores are S^T = K Q^T with mma.sync m16n8k16 (16 tokens
+//    x 8 query-head columns); the online softmax runs in the exp2 domain on the
+//    fragments; P^T is turned into the B operand with movmatrix; O^T += V^T P
+//    accumulates in registers.
 //  * Fused options: the q prologue (head RMSNorm + RoPE of q), the K/V append of the
 //    new token (head RMSNorm + RoPE of k written into its page slot before the
-//    producer loads that stage), and the sigmoid output gate.
+//    stage holding it is copied), and the sigmoid output gate.
 //  * The splits of a kv head form thread-block clusters. Each CTA leaves its (o, lse)
 //    partial in shared memory; after a cluster barrier every CTA merges one slice of
 //    the outputs from all partials of its cluster through distributed shared memory.
@@ -53,9 +56,9 @@ struct AttnShape {
   static constexpr int kRing = (D == 64) ? 8 : 4;
   static_assert(kRing % kConsumerWarps == 0, "a ring slot must always be consumed by the same warp");
   static constexpr int kRingBytes = kRing * kStageBytes;        // 64 KB
-  static constexpr int kCombineBytes = kConsumerWarps * (kMaxGroup * D + 2 * kMaxGroup) * 4;
+  static constexpr int kCombineBytes = kConsumerWarps * (kMaxGroup * (D + 4) + 2 * kMaxGroup) * 4;
   static_assert(kCombineBytes + (kMaxGroup * (D + 1) + 4) * 4 <= kRingBytes, "combine buffer + partial");
-  static constexpr int kCtrlBytes = 8 * (2 * kRing + 2);        // full[], empty[], append barrier, pad
+  static constexpr int kCtrlBytes = 128;                         // full[] barriers
   static constexpr int kQBytes = kMaxGroup * D * 2;
   static constexpr int kFlagBytes = 64;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes;
@@ -105,7 +108,7 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __grid_constant__ AttnParams p) {
   using Sh = AttnShape<D>;
   constexpr int kRing = Sh::kRing;
   constexpr int TOK = Sh::kTok;
@@ -116,8 +119,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + Sh::kRingBytes);
-  uint64_t* empty = full + kRing;
-  uint64_t* append_bar = empty + kRing;
   T* q_s = reinterpret_cast<T*>(ring + Sh::kRingBytes + Sh::kCtrlBytes);
   volatile int* flags_s = reinterpret_cast<volatile int*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes);
   // flags_s[0]: abort, flags_s[1]: this CTA merges
@@ -163,11 +164,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
-    for (int i = 0; i < kRing; ++i) {
-      mbar_init(&full[i], kProducerWarps);
-      mbar_init(&empty[i], 1);
-    }
-    mbar_init(append_bar, 1);
+    for (int i = 0; i < kRing; ++i) mbar_init(&full[i], 1);
     flags_s[0] = 0;
     flags_s[1] = 0;
     fence_mbar_init();
@@ -175,105 +172,65 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp >= kConsumerWarps) {
-    // ======================= producer warps =======================
-    // warp kConsumerWarps issues the K copies of every stage, the next warp the V copies
-    const int pw = warp - kConsumerWarps;
-    const uint64_t pol = l2_policy_evict_first();
-    if (lane == 0) tma_prefetch_desc(pw == 0 ? &p.tm_k : &p.tm_v);
-    const CUtensorMap* tmap = pw == 0 ? &p.tm_k : &p.tm_v;
-    const int bh = p.box_h;
-    const int box_bytes = bh * D * 2;    // all chunks of bh token rows
-    const int P = p.page_size;
-    const int npages = table != nullptr ? (S + P - 1) / P : 0;
-    // page-table windows: lane l holds entry wbase + l in `cur` and wbase + 32 + l in `nxt`
-    int wbase = 0, cur = 0, nxt = 0;
-    if (table != nullptr) {
-      wbase = (st_lo * TOK) / P;
-      const int e0 = wbase + lane, e1 = wbase + 32 + lane;
-      cur = e0 < npages ? __ldg(table + e0) : 0;
-      nxt = e1 < npages ? __ldg(table + e1) : 0;
+  // ---- stage copies: every warp streams its own ring slots ----
+  // Stage i of this CTA lives in slot i % kRing and is consumed by warp i % 4, which
+  // also issues the slot's next stage (i + kRing) as soon as it has finished with it,
+  // so a slot never waits on another warp. Lane l < 16 copies K box l of a stage and
+  // lane 16 + l the V box l; a box is every 64-element chunk of bh token rows, at
+  // row page_table[t/P]*P + t%P when paged. The page-table entries of the warp's next
+  // stage are loaded one stage ahead.
+  const uint64_t pol = l2_policy_evict_first();
+  if (lane == 0) {
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+  }
+  const int bh = p.box_h;
+  const int lbh = p.log2_box_h;
+  const int box_bytes = bh * D * 2;  // all chunks of bh token rows
+  const int P = p.page_size;
+  const int bx = lane & 15;
+  const CUtensorMap* tmap = lane < 16 ? &p.tm_k : &p.tm_v;
+  const int kv_off = lane < 16 ? 0 : Sh::kKBytes;
+  const int append_stage = do_append ? nst - 1 : -1;
+  // page-table entry holding box bx of stage j, or -1
+  auto box_entry = [&](int j) -> int {
+    const int tb = (st_lo + j) * TOK + bx * bh;
+    return (j < nst && bx * bh < TOK && tb < S) ? tb / P : -1;
+  };
+  auto load_entry = [&](int e) -> int { return e >= 0 ? __ldg(table + e) : 0; };
+  auto issue = [&](int j, int page) {
+    const int slot = j % kRing;
+    const int t0 = (st_lo + j) * TOK;
+    const int nbox = (min(TOK, S - t0) + bh - 1) / bh;
+    const int tb = t0 + bx * bh;
+    long long row = tb;
+    if (table != nullptr && bx < nbox) {
+      const int e = tb / P;
+      row = static_cast<long long>(page) * P + (tb - e * P);
+      if (page < 0 || (p.cache_tokens > 0 && row + bh > p.cache_tokens)) {
+        record_status(p.status, QIC_DEV_BAD_PAGE);
+        row = tb - e * P;  // clamp to page 0
+      }
     }
-    // lane l copies box l of a stage: every 64-element chunk of bh token rows
-    const int op_box = lane;
-    const int kv_off = pw * Sh::kKBytes;
-    int issued = 0;
-    bool ok = true;
-#pragma unroll 1
-    for (int i = 0; i < nst; ++i) {
-      const int slot = i % kRing;
-      if (i >= kRing) {
-        if (!__all_sync(kFullMask, mbar_wait(&empty[slot], ((i / kRing) - 1) & 1, deadline))) {
-          ok = false;
-          break;
-        }
-      }
-      if (__shfl_sync(kFullMask, flags_s[0], 0)) {
-        ok = false;
-        break;
-      }
-      const int t0 = (st_lo + i) * TOK;
-      const int nvalid = min(TOK, S - t0);
-      if (do_append && i == nst - 1) {
-        // the stage holding the new token is loaded after the append has landed
-        if (!__all_sync(kFullMask, mbar_wait(append_bar, 0, deadline))) {
-          ok = false;
-          break;
-        }
-      }
-      const int nbox = (nvalid + bh - 1) / bh;
-      const int nops = nbox;  // copies of this warp
-      const int jb = min(op_box, nbox - 1);
-      const int tb = t0 + jb * bh;
-      int row = tb;
-      if (table != nullptr) {
-        const int e_first = t0 / P;
-        while (e_first >= wbase + 32) {  // uniform across the warp
-          cur = nxt;
-          wbase += 32;
-          const int en = wbase + 32 + lane;
-          nxt = en < npages ? __ldg(table + en) : 0;
-        }
-        const int e = tb / P;
-        const int src = e - wbase;  // < 64: a stage spans at most 5 pages of >= 8 tokens
-        const int v0 = __shfl_sync(kFullMask, cur, src & 31);
-        const int v1 = __shfl_sync(kFullMask, nxt, src & 31);
-        const int page = src < 32 ? v0 : v1;
-        long long r = static_cast<long long>(page) * P + (tb - e * P);
-        if (lane < nops && (page < 0 || (p.cache_tokens > 0 && r + bh > p.cache_tokens))) {
-          record_status(p.status, QIC_DEV_BAD_PAGE);
-          r = tb - e * P;  // clamp to page 0
-        }
-        row = static_cast<int>(r);
-      }
-      uint8_t* sk = ring + slot * Sh::kStageBytes;
-      // each producer warp posts the bytes of its own copies before issuing them
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * box_bytes));
-      __syncwarp();
-      if (lane < nops) {
-        uint8_t* dst = sk + kv_off + op_box * box_bytes;
-        tma_load_3d(dst, tmap, &full[slot], 0, row, kvh * Sh::kChunks, pol);
-      }
-      issued = i + 1;
-      __syncwarp();
-    }
-    if (!ok && lane == 0) {
-      record_status(p.status, QIC_DEV_TIMEOUT);
-      flags_s[0] = 1;
-      // wait (bounded) for the copies this CTA still has in flight
-      const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
-      for (int i = max(0, issued - kRing); i < issued; ++i) mbar_wait(&full[i % kRing], (i / kRing) & 1, dl2);
-    }
+    if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(2 * nbox * box_bytes));
     __syncwarp();
-    if (nsplit > 1) {
-      // every thread of the cluster takes part in the consumers' two cluster barriers
-      cluster_sync_all();
-      cluster_sync_all();
+    if (bx < nbox) {
+      // this warp's earlier shared-memory reads of the slot precede the copy's writes
+      fence_proxy_async_smem();
+      tma_load_3d(ring + slot * Sh::kStageBytes + kv_off + bx * box_bytes, tmap, &full[slot], 0,
+                  static_cast<int>(row), kvh * Sh::kChunks, pol);
     }
-    return;
+  };
+  int next = warp;  // next stage this warp issues
+  int pg = table != nullptr ? load_entry(box_entry(next)) : 0;
+  // initial fill, before the inputs of the preceding kernel are waited for; the stage
+  // holding the appended token waits for the append
+  while (next < nst && next < kRing && next != append_stage) {
+    issue(next, pg);
+    next += kConsumerWarps;
+    if (table != nullptr) pg = load_entry(box_entry(next));
   }
 
-  // ======================= consumer warps =======================
   const int ctid = threadIdx.x;  // 0..127
   const int hd = p.head_dim;
   const T* qb = static_cast<const T*>(p.q) + static_cast<size_t>(b) * p.q_bstride;
@@ -316,13 +273,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
         } else if (lane == 0) {
           record_status(p.status, QIC_DEV_BAD_PAGE);
         }
+        // the stage holding this row is copied by TMA (async proxy) after the barrier below
         fence_proxy_async_global();
         __syncwarp();
-        if (lane == 0) mbar_arrive(append_bar);
       }
     }
   }
   consumer_sync();
+  // the rest of the initial fill: the stage holding the appended token
+  while (next < nst && next < kRing) {
+    fence_proxy_async_global();
+    issue(next, pg);
+    next += kConsumerWarps;
+    if (table != nullptr) pg = load_entry(box_entry(next));
+  }
 
   // ---- B fragments of Q^T (k = dims, n = query heads of the group) ----
   const int hq = lane >> 2;       // n index held by this lane in B fragments
@@ -340,9 +304,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   }
 
   // ---- per-lane shared-memory address pieces (swizzled, chunk-major boxes) ----
-  const int bh = p.box_h;
-  const int lbh = p.log2_box_h;
-  const int box_bytes = bh * D * 2;
   const int box_row_bytes = bh * 128;
   const int q8 = lane >> 3;  // ldmatrix matrix index supplied by this lane
   const int rr = lane & 7;   // row within that 8x8 matrix
@@ -363,9 +324,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   const float sl2 = p.scale_log2;
   bool ok = true;
+  int i = warp;
 
 #pragma unroll 1
-  for (int i = warp; i < nst; i += kConsumerWarps) {
+  for (; i < nst; i += kConsumerWarps) {
     const int slot = i % kRing;
     if (!__all_sync(kFullMask, mbar_wait(&full[slot], (i / kRing) & 1, deadline))) {
       ok = false;
@@ -471,11 +433,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    // refill this slot with the warp's next stage (i + kRing) right away
+    if (next < nst) {
+      issue(next, pg);
+      next += kConsumerWarps;
+      if (table != nullptr) pg = load_entry(box_entry(next));
+    }
   }
-  if (!ok && lane == 0) {
-    record_status(p.status, QIC_DEV_TIMEOUT);
-    flags_s[0] = 1;
+  if (!ok) {
+    if (lane == 0) {
+      record_status(p.status, QIC_DEV_TIMEOUT);
+      flags_s[0] = 1;
+    }
+    // wait (bounded) for this warp's copies still in flight before the CTA exits
+    const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
+#pragma unroll 1
+    for (int j = i; j < next; j += kConsumerWarps) mbar_wait(&full[j % kRing], (j / kRing) & 1, dl2);
+    __syncwarp();
   }
   // full row sums per head column
 #pragma unroll
@@ -486,58 +460,70 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   consumer_sync();
   const bool aborted = flags_s[0] != 0;
 
-  // ---- combine the four consumer warps (ring memory is free now) ----
+  // ---- combine the four warps (ring memory is free now) ----
+  // Each warp's share of head h is weighted by exp2(m_w - M) / L with M, L the
+  // head's maximum and normaliser over the four warps; the weights are applied to
+  // the accumulators in registers, so the cross-warp step is a plain sum.
   float* cm = reinterpret_cast<float*>(ring);  // [4][8] m
   float* cl = cm + kConsumerWarps * 8;         // [4][8] l
-  float* co = cl + kConsumerWarps * 8;         // [4][8][D] o
+  float* co = cl + kConsumerWarps * 8;         // [4][8][D + 4] weighted o (padded rows: no bank conflicts)
   float* mine = reinterpret_cast<float*>(ring + Sh::kCombineBytes);  // this split: [o: G*D][lse: G]
+  constexpr int kCoRow = D + 4;
+  const int hA = (lane & 3) * 2, hB = hA + 1;
   if (!aborted) {
-    const int hA = (lane & 3) * 2, hB = hA + 1;
     if (lane < 4) {
       cm[warp * 8 + hA] = m0;
       cm[warp * 8 + hB] = m1;
       cl[warp * 8 + hA] = l0;
       cl[warp * 8 + hB] = l1;
     }
+  }
+  consumer_sync();
+  if (!aborted) {
+    float MA = -INFINITY, MB = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      MA = fmaxf(MA, cm[w * 8 + hA]);
+      MB = fmaxf(MB, cm[w * 8 + hB]);
+    }
+    const float MAu = (MA == -INFINITY) ? 0.0f : MA, MBu = (MB == -INFINITY) ? 0.0f : MB;
+    float LA = 0.0f, LB = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      LA += cl[w * 8 + hA] * exp2f(cm[w * 8 + hA] - MAu);
+      LB += cl[w * 8 + hB] * exp2f(cm[w * 8 + hB] - MBu);
+    }
+    const float wA = LA > 0.0f ? exp2f(m0 - MAu) / LA : 0.0f;
+    const float wB = LB > 0.0f ? exp2f(m1 - MBu) / LB : 0.0f;
+    float* coA = co + (warp * 8 + hA) * kCoRow + hq;
+    float* coB = co + (warp * 8 + hB) * kCoRow + hq;
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
-      const int d0 = j * 16 + hq;
-      co[(warp * 8 + hA) * D + d0] = acc[j][0];
-      co[(warp * 8 + hB) * D + d0] = acc[j][1];
-      co[(warp * 8 + hA) * D + d0 + 8] = acc[j][2];
-      co[(warp * 8 + hB) * D + d0 + 8] = acc[j][3];
+      coA[j * 16] = acc[j][0] * wA;
+      coB[j * 16] = acc[j][1] * wB;
+      coA[j * 16 + 8] = acc[j][2] * wA;
+      coB[j * 16 + 8] = acc[j][3] * wB;
+    }
+    // this split's log-sum-exp per head (log2 domain)
+    if (warp == 0 && lane < 4 && nsplit > 1) {
+      if (hA < G) mine[G * D + hA] = LA > 0.0f ? MAu + log2f(LA) : -INFINITY;
+      if (hB < G) mine[G * D + hB] = LB > 0.0f ? MBu + log2f(LB) : -INFINITY;
     }
   }
   consumer_sync();
   const size_t qoff = static_cast<size_t>(kvh) * G * D;  // first output row of this group
   const int GD = G * D;
   if (!aborted) {
-#pragma unroll 1
+#pragma unroll 2
     for (int idx = ctid; idx < GD; idx += kConsumerWarps * 32) {
-      const int h = idx / D;
-      float M = -INFINITY;
+      const int h = idx / D, d = idx - h * D;
+      float o = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cm[w * 8 + h]);
-      const float Mu = (M == -INFINITY) ? 0.0f : M;
-      float L = 0.0f, O = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float wt = exp2f(cm[w * 8 + h] - Mu);
-        L += cl[w * 8 + h] * wt;
-        O += co[(w * 8 + h) * D + (idx - h * D)] * wt;
-      }
+      for (int w = 0; w < kConsumerWarps; ++w) o += co[(w * 8 + h) * kCoRow + d];
       if (nsplit == 1) {
-        const float inv_l = 1.0f / fmaxf(L, 1e-12f);
-        T ot = from_f32<T>(O * inv_l);
-        if (gb != nullptr) {
-          const float g = to_f32<T>(gb[qoff + idx]);
-          const float sig = 1.0f / (1.0f + expf(-g));
-          ot = from_f32<T>(to_f32<T>(ot) * sig);
-        }
-        ob[qoff + idx] = ot;
+        write_out<T>(ob, gb, qoff + idx, o);
       } else {
-        mine[idx] = (L > 0.0f) ? O / L : 0.0f;
-        if (idx - h * D == 0) mine[GD + h] = (L > 0.0f) ? Mu + log2f(L) : -INFINITY;
+        mine[idx] = o;
       }
     }
   }
@@ -552,22 +538,33 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
-  float* gslot = p.part + static_cast<size_t>(part_base + cid) * partial_floats(G, D);  // [o: G*D][lse: G]
+  const int pf = partial_floats(G, D);
+  float* gslot = p.part + static_cast<size_t>(part_base + cid) * pf;  // [o: G*D][lse: G]
 #pragma unroll 1
   for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
     const int h = idx / D;
-    float lse_c[kMaxCluster];
-    float mx = -INFINITY;
-    for (int c = 0; c < C; ++c) {
-      lse_c[c] = *cluster_map(mine + GD + h, c);
-      mx = fmaxf(mx, lse_c[c]);
+    // all remote loads are issued before any is used: one DSMEM round trip
+    float lse_c[kMaxCluster], o_c[kMaxCluster];
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < C) {
+        lse_c[c] = *cluster_map(mine + GD + h, c);
+        o_c[c] = *cluster_map(mine + idx, c);
+      }
     }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c)
+      if (c < C) mx = fmaxf(mx, lse_c[c]);
     const float mxu = (mx == -INFINITY) ? 0.0f : mx;
     float sum = 0.0f, o = 0.0f;
-    for (int c = 0; c < C; ++c) {
-      const float w = exp2f(lse_c[c] - mxu);
-      sum += w;
-      o += w * *cluster_map(mine + idx, c);
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < C) {
+        const float w = exp2f(lse_c[c] - mxu);
+        sum += w;
+        o += w * o_c[c];
+      }
     }
     o = sum > 0.0f ? o / sum : 0.0f;
     if (nclust == 1) {
@@ -577,6 +574,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
       if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
     }
   }
+  // every CTA of the cluster has read the partials it needs from this one
+  cluster_sync_all();
   if (nclust > 1) {
     // ---- merge the cluster partials of this slice: last arriving cluster ----
     consumer_sync();
@@ -587,27 +586,36 @@ __global__ void __launch_bounds__(kAttnThreads, 2) decode_attn_kernel(const __gr
     }
     consumer_sync();
     if (flags_s[1]) {
-      const float* g0 = p.part + static_cast<size_t>(part_base) * partial_floats(G, D);
-      const int pf = partial_floats(G, D);
+      const float* g0 = p.part + static_cast<size_t>(part_base) * pf;
 #pragma unroll 1
       for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
         const int h = idx / D;
-        float mx = -INFINITY;
-        for (int k = 0; k < nclust; ++k) mx = fmaxf(mx, __ldcg(g0 + static_cast<size_t>(k) * pf + GD + h));
-        const float mxu = (mx == -INFINITY) ? 0.0f : mx;
-        float sum = 0.0f, o = 0.0f;
-        for (int k = 0; k < nclust; ++k) {
-          const float w = exp2f(__ldcg(g0 + static_cast<size_t>(k) * pf + GD + h) - mxu);
-          sum += w;
-          o += w * __ldcg(g0 + static_cast<size_t>(k) * pf + idx);
+        // online log-sum-exp over the cluster partials, four loads in flight at a time
+        float mx = -INFINITY, sum = 0.0f, o = 0.0f;
+#pragma unroll 1
+        for (int k0 = 0; k0 < nclust; k0 += 4) {
+          float lk[4], ok[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u;
+            lk[u] = k < nclust ? __ldcg(g0 + static_cast<size_t>(k) * pf + GD + h) : -INFINITY;
+            ok[u] = k < nclust ? __ldcg(g0 + static_cast<size_t>(k) * pf + idx) : 0.0f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float mn = fmaxf(mx, lk[u]);
+            if (mn == -INFINITY) continue;
+            const float sc = exp2f(mx - mn), w = exp2f(lk[u] - mn);
+            sum = sum * sc + w;
+            o = o * sc + w * ok[u];
+            mx = mn;
+          }
         }
         write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
       }
       if (ctid == 0) p.counters[counter] = 0;  // ready for the next call
     }
   }
-  // keep this CTA's shared memory alive until every CTA of the cluster has read it
-  cluster_sync_all();
 }
 
 // ----------------------------------------------------------------------------

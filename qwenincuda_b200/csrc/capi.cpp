@@ -298,7 +298,7 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
     // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
     if (cluster == 0) cluster = 8;
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
-    if (max_clusters <= 0) max_clusters = (2 * sm_count()) / cluster;
+    if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     int nclust = std::max(1, max_clusters / Hkv);
     n_splits = cluster * nclust;
     if (n_splits > n_stages) {

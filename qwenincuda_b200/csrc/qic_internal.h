@@ -10,9 +10,8 @@
 
 namespace qic {
 
-constexpr int kConsumerWarps = 4;    // warps that run the mma pipeline
-constexpr int kProducerWarps = 2;    // warps issuing TMA copies (K copies / V copies)
-constexpr int kAttnThreads = (kConsumerWarps + kProducerWarps) * 32;
+constexpr int kConsumerWarps = 4;    // warps of an attention CTA; each streams and consumes its own ring slots
+constexpr int kAttnThreads = kConsumerWarps * 32;
 constexpr int kMaxCluster = 16;      // CTAs of one (sequence, kv head) merged through DSMEM
 constexpr int kMaxGroup = 8;         // query heads per kv head handled by one n8 mma tile
 constexpr int kMaxSplits = 256;      // KV splits per kv head
