@@ -215,8 +215,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(2 * nbox * box_bytes));
     __syncwarp();
     if (bx < nbox) {
-      // this warp's earlier shared-memory reads of the slot precede the copy's writes
-      fence_proxy_async_smem();
+      // the warp's ldmatrix reads of this slot have completed: their results fed the
+      // mma instructions issued before this copy
       tma_load_3d(ring + slot * Sh::kStageBytes + kv_off + bx * box_bytes, tmap, &full[slot], 0,
                   static_cast<int>(row), kvh * Sh::kChunks, pol);
     }
