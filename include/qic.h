@@ -3,8 +3,9 @@
  *
  * Plain C types only: device pointers as void*, sizes as int32/int64, CUDA streams
  * as an opaque pointer (binary-compatible with cudaStream_t / CUstream). Every entry
- * point returns a qic_status (0 = success) and never allocates device memory;
- * scratch space is passed in by the caller (see qic_decode_workspace_bytes).
+ * point returns a qic_status (0 = success) and, except qic_device_alloc, never
+ * allocates device memory; scratch space is passed in by the caller (see
+ * qic_decode_workspace_bytes).
  *
  * Element types: QIC_DTYPE_F16 (the reference's `half`) or QIC_DTYPE_BF16.
  *
@@ -58,11 +59,20 @@ enum {
 enum {
   QIC_FUSE_Q_PROLOGUE = 1,       /* q := RoPE(head_rmsnorm(q, q_norm_w)) inside the attention kernel */
   QIC_FUSE_APPEND = 2,           /* k_new/v_new appended at position seq_len-1 inside the kernel */
-  QIC_PDL = 4                    /* programmatic dependent launch: the kernel may start while the previous
+  QIC_PDL = 4,                   /* programmatic dependent launch: the kernel may start while the previous
                                     kernel in the stream runs and prefetch cached K/V rows (all but the
                                     appended one) and page-table entries; q, k_new, v_new, gate and the
                                     workspace are touched only after that kernel has completed. The
                                     previous kernel must not write the page table or those cached rows. */
+  QIC_PARTIAL_OUT = 8,           /* out is float [Hkv][qic_partial_floats()]: per kv head, the G*d
+                                    outputs normalised by their own softmax sum, then G log-sum-exp
+                                    values (log2 of the sum of 2^(score*log2(e)/sqrt(d))), padded to a
+                                    multiple of 4 floats; no gate. Partials of disjoint token ranges
+                                    of one sequence combine with qic_attention_merge. */
+  QIC_EXPLICIT_POSITION = 16     /* args->position is the token position used for RoPE of q and of the
+                                    appended k (default seq_len-1). The append still writes the last
+                                    attended row (index seq_len-1 of this call's cache or page table):
+                                    a rank that holds the final shard of a longer sequence. */
 };
 
 const char* qic_status_string(int status);
@@ -131,6 +141,7 @@ typedef struct qic_decode_args {
   int32_t num_splits;       /* KV splits per kv head; 0 = chosen from the SM count */
   int32_t cluster_size;     /* splits merged on chip per thread-block cluster (1..16, divides
                                num_splits); 0 = chosen with num_splits */
+  int64_t position;         /* QIC_EXPLICIT_POSITION: RoPE position of q and the appended k */
 } qic_decode_args;
 
 /* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len). */
@@ -163,6 +174,64 @@ int qic_decode_attention_noalloc(const qic_decode_args* args, qic_stream_t strea
 
 /* Size in bytes of the array qic_decode_attention_noalloc uses. */
 size_t qic_noalloc_scratch_bytes(void);
+
+/* Floats per kv head of a QIC_PARTIAL_OUT partial: ((H/Hkv)*(d+1)+3) & ~3. */
+size_t qic_partial_floats(int num_heads, int num_kv_heads, int head_dim);
+
+/* out[h,:] = log-sum-exp merge of num_partials QIC_PARTIAL_OUT partials of one
+ * sequence (stacked [num_partials][Hkv][qic_partial_floats]), each over a disjoint set
+ * of tokens, then the optional gate (out *= sigmoid(gate)); out is [H, d] of dtype.
+ * The partial/merge pair gives the all-gather form of context parallelism (partials
+ * exchanged by a collective library); qic_cp_decode_attention fuses the exchange. */
+int qic_attention_merge(int dtype, const float* partials, int num_partials, int num_heads, int num_kv_heads,
+                        int head_dim, const void* gate, void* out, qic_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Context parallelism: one sequence's K/V split across GPUs.                 */
+/* No counterpart in the reference (single GPU); the shards' partials are      */
+/* exchanged over NVLink inside the attention kernel and merged by log-sum-exp. */
+/* ------------------------------------------------------------------------- */
+
+#define QIC_MAX_RANKS 8
+#define QIC_IPC_HANDLE_BYTES 64
+
+typedef struct qic_cp_args {
+  int32_t rank;             /* this GPU's shard, 0 <= rank < world */
+  int32_t world;            /* shards of the sequence, 1..QIC_MAX_RANKS */
+  void* exchange;           /* this rank's exchange buffer, qic_cp_exchange_bytes, zeroed before first use */
+  size_t exchange_bytes;
+  void* peer_exchange[QIC_MAX_RANKS]; /* every rank's exchange buffer as addressable from this process
+                                         (peer memory opened with qic_ipc_open_handle);
+                                         peer_exchange[rank] == exchange */
+  int32_t timeout_ms;       /* bound of the device-side wait for the other ranks (0 = 2000 ms) */
+  int32_t reserved;
+} qic_cp_args;
+
+/* Bytes of one rank's exchange buffer. */
+size_t qic_cp_exchange_bytes(int num_heads, int num_kv_heads, int head_dim, int world);
+
+/* Decode attention of one shard of a sequence, fused with the exchange: the CTA that
+ * holds a slice of this rank's merged partial stores it into every rank's exchange
+ * buffer over NVLink and raises a flag there, waits (bounded) for the same slice from
+ * every other rank, merges the world partials by log-sum-exp and writes out (with the
+ * gate). Every rank calls it once per step with the same shapes, cluster size (8)
+ * and number of calls; args->workspace is required (it keeps the call epoch).
+ * Shard layout: each rank's args describe its own tokens (seq_len, page_table or
+ * contiguous rows); q is the same on every rank; QIC_EXPLICIT_POSITION gives the
+ * global position for RoPE; the rank holding the last token sets QIC_FUSE_APPEND.
+ * A peer that does not publish within timeout_ms sets QIC_DEV_PEER_TIMEOUT in the
+ * device status word; the kernel then returns without writing out. */
+int qic_cp_decode_attention(const qic_decode_args* args, const qic_cp_args* cp, qic_stream_t stream);
+
+/* Device memory for exchange buffers: cudaMalloc'd and zeroed (an IPC handle must
+ * name the start of an allocation). */
+int qic_device_alloc(size_t bytes, void** ptr);
+int qic_device_free(void* ptr);
+/* CUDA IPC: handle (QIC_IPC_HANDLE_BYTES) of a qic_device_alloc buffer, and the
+ * mapping of another process's buffer into this one (peer access enabled). */
+int qic_ipc_get_handle(const void* ptr, void* handle);
+int qic_ipc_open_handle(const void* handle, void** ptr);
+int qic_ipc_close_handle(void* ptr);
 
 /* ------------------------------------------------------------------------- */
 /* Batched paged decode over one shared page pool.                            */

@@ -14,6 +14,10 @@ QIC_DEV_BAD_PAGE = 2
 QIC_DEV_PEER_TIMEOUT = 4
 QIC_DEV_BAD_PLAN = 8
 QIC_PDL = 4
+QIC_PARTIAL_OUT = 8
+QIC_EXPLICIT_POSITION = 16
+QIC_MAX_RANKS = 8
+QIC_IPC_HANDLE_BYTES = 64
 
 STATUS_NAMES = {
     0: "QIC_SUCCESS",
@@ -72,6 +76,21 @@ class DecodeArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("num_splits", ctypes.c_int32),
         ("cluster_size", ctypes.c_int32),
+        ("position", ctypes.c_int64),
+    ]
+
+
+class CpArgs(ctypes.Structure):
+    """Mirror of qic_cp_args."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("exchange", ctypes.c_void_p),
+        ("exchange_bytes", ctypes.c_size_t),
+        ("peer_exchange", ctypes.c_void_p * QIC_MAX_RANKS),
+        ("timeout_ms", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -168,6 +187,16 @@ SIGNATURES = {
     "qic_batch_decode_attention": (ctypes.c_int, [ctypes.POINTER(BatchDecodeArgs), _vp]),
     "qic_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
     "qic_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "qic_partial_floats": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qic_attention_merge": (
+        ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
+    "qic_cp_exchange_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qic_cp_decode_attention": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(CpArgs), _vp]),
+    "qic_device_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "qic_device_free": (ctypes.c_int, [_vp]),
+    "qic_ipc_get_handle": (ctypes.c_int, [_vp, _vp]),
+    "qic_ipc_open_handle": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "qic_ipc_close_handle": (ctypes.c_int, [_vp]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -104,6 +104,16 @@ __device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, float o)
   ob[i] = ot;
 }
 
+// Slot of the exchange buffer at `base` for (parity, source rank, kv head): flag of
+// slice c, and the partial [o: G*D][lse: G].
+__device__ __forceinline__ unsigned* cp_flag(void* base, int par, int src, int world, int Hkv, int kvh, int c) {
+  return static_cast<unsigned*>(base) + ((static_cast<size_t>(par) * world + src) * Hkv + kvh) * kCpSlices + c;
+}
+__device__ __forceinline__ float* cp_data(void* base, int par, int src, int world, int Hkv, int kvh, int pf) {
+  return reinterpret_cast<float*>(static_cast<char*>(base) + cp_flags_bytes(Hkv, world)) +
+         ((static_cast<size_t>(par) * world + src) * Hkv + kvh) * pf;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -236,6 +246,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const T* qb = static_cast<const T*>(p.q) + static_cast<size_t>(b) * p.q_bstride;
   const T* gb = p.gate != nullptr ? static_cast<const T*>(p.gate) + static_cast<size_t>(b) * p.q_bstride : nullptr;
   T* ob = static_cast<T*>(p.out) + static_cast<size_t>(b) * p.q_bstride;
+  // RoPE position of q and of the appended k: the last attended token, or the
+  // caller's global position when this launch holds one shard of a longer sequence
+  const int rpos = (p.plan == nullptr && p.rope_pos >= 0) ? static_cast<int>(p.rope_pos) : S - 1;
   // inputs written by the preceding kernel are read only after it has completed
   pdl_wait();
   // ---- prologue: q rows into shared memory, and the fused append ----
@@ -248,7 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         row_load<T, D>(qb + static_cast<size_t>(kvh * G + r) * D, v, lane);
         if (p.flags & QIC_FUSE_Q_PROLOGUE) {
           row_rmsnorm<T, D>(v, static_cast<const T*>(p.q_norm_w), hd, p.eps, lane);
-          row_rope<T, D>(v, hd, S - 1, p.theta, lane);
+          row_rope<T, D>(v, hd, rpos, p.theta, lane);
         }
         row_store<T, D>(q_s + r * D, v, lane);
       } else {
@@ -266,7 +279,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
           float vv[D / 32];
           row_load<T, D>(static_cast<const T*>(p.v_new) + nb, vv, lane);
           row_rmsnorm<T, D>(v, static_cast<const T*>(p.k_norm_w), hd, p.eps, lane);
-          row_rope<T, D>(v, hd, pos, p.theta, lane);
+          row_rope<T, D>(v, hd, rpos, p.theta, lane);
           const size_t at = static_cast<size_t>(slot) * kv_dim + static_cast<size_t>(kvh) * D;
           row_store<T, D>(static_cast<T*>(p.k_cache) + at, v, lane);
           row_store<T, D>(static_cast<T*>(p.v_cache) + at, vv, lane);
@@ -505,7 +518,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       coB[j * 16 + 8] = acc[j][3] * wB;
     }
     // this split's log-sum-exp per head (log2 domain)
-    if (warp == 0 && lane < 4 && nsplit > 1) {
+    if (warp == 0 && lane < 4 && (nsplit > 1 || p.part_out != nullptr)) {
       if (hA < G) mine[G * D + hA] = LA > 0.0f ? MAu + log2f(LA) : -INFINITY;
       if (hB < G) mine[G * D + hB] = LB > 0.0f ? MBu + log2f(LB) : -INFINITY;
     }
@@ -513,6 +526,27 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   consumer_sync();
   const size_t qoff = static_cast<size_t>(kvh) * G * D;  // first output row of this group
   const int GD = G * D;
+  const int pf = partial_floats(G, D);
+  const bool cp = p.cp_world > 0;
+  unsigned cp_e = 0;  // exchange epoch of this call (slice mergers, context parallel)
+  // Destination of the final value o of output idx (head h, log-sum-exp lse): the
+  // output, the caller's fp32 partial (QIC_PARTIAL_OUT), or the slot of this rank in
+  // every rank's exchange buffer.
+  auto emit = [&](int idx, int h, float o, float lse, bool head_first) {
+    if (p.part_out != nullptr) {
+      float* po = p.part_out + static_cast<size_t>(kvh) * pf;
+      po[idx] = o;
+      if (head_first) po[GD + h] = lse;
+    } else if (cp) {
+      for (int r = 0; r < p.cp_world; ++r) {
+        float* dst = cp_data(p.cp_peer[r], cp_e & 1, p.cp_rank, p.cp_world, p.Hkv, kvh, pf);
+        dst[idx] = o;
+        if (head_first) dst[GD + h] = lse;
+      }
+    } else {
+      write_out<T>(ob, gb, qoff + idx, o);
+    }
+  };
   if (!aborted) {
 #pragma unroll 2
     for (int idx = ctid; idx < GD; idx += kConsumerWarps * 32) {
@@ -521,7 +555,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) o += co[(w * 8 + h) * kCoRow + d];
       if (nsplit == 1) {
-        write_out<T>(ob, gb, qoff + idx, o);
+        emit(idx, h, o, mine[GD + h], d == 0);
       } else {
         mine[idx] = o;
       }
@@ -538,7 +572,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
-  const int pf = partial_floats(G, D);
+  if (cp && nclust == 1) cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
   float* gslot = p.part + static_cast<size_t>(part_base + cid) * pf;  // [o: G*D][lse: G]
 #pragma unroll 1
   for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
@@ -568,7 +602,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     o = sum > 0.0f ? o / sum : 0.0f;
     if (nclust == 1) {
-      write_out<T>(ob, gb, qoff + idx, o);
+      emit(idx, h, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY, idx == lo || idx - h * D == 0);
     } else {
       gslot[idx] = o;
       if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
@@ -586,6 +620,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     consumer_sync();
     if (flags_s[1]) {
+      if (cp) cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
       const float* g0 = p.part + static_cast<size_t>(part_base) * pf;
 #pragma unroll 1
       for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
@@ -611,11 +646,129 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
             mx = mn;
           }
         }
-        write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
+        emit(idx, h, sum > 0.0f ? o / sum : 0.0f, sum > 0.0f ? mx + log2f(sum) : -INFINITY,
+             idx == lo || idx - h * D == 0);
       }
       if (ctid == 0) p.counters[counter] = 0;  // ready for the next call
     }
   }
+  if (cp && (nclust == 1 || flags_s[1] != 0)) {
+    // ---- context parallel: publish this slice to every rank, wait for theirs, merge ----
+    // The cluster has 8 CTAs (kCpSlices) on every rank, so slice `rank` covers the same
+    // outputs [lo, hi) everywhere.
+    const int W = p.cp_world, par = cp_e & 1;
+    if (ctid == 0) flags_s[2] = 0;
+    consumer_sync();  // every thread's stores of this slice are issued
+    if (ctid == 0) {
+      fence_acq_rel_sys();
+      for (int r = 0; r < W; ++r) st_relaxed_sys_u32(cp_flag(p.cp_peer[r], par, p.cp_rank, W, p.Hkv, kvh, rank), cp_e);
+    }
+    if (ctid < W) {
+      const unsigned* f = cp_flag(p.cp_peer[p.cp_rank], par, ctid, W, p.Hkv, kvh, rank);
+      const uint64_t dl = globaltimer_ns() + p.timeout_ns;
+      bool ok = false;
+#pragma unroll 1
+      for (uint32_t it = 0;; ++it) {
+        if (ld_acquire_sys_u32(f) == cp_e) {
+          ok = true;
+          break;
+        }
+        if ((it & 15u) == 0 && globaltimer_ns() > dl) break;
+        __nanosleep(64);
+      }
+      if (!ok) {
+        record_status(p.status, QIC_DEV_PEER_TIMEOUT);
+        flags_s[2] = 1;
+      }
+    }
+    consumer_sync();
+    if (flags_s[2] == 0 && !aborted) {
+#pragma unroll 1
+      for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
+        const int h = idx / D;
+        float lr[kMaxRanks], orr[kMaxRanks];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+          if (r < W) {
+            const float* src = cp_data(p.cp_peer[p.cp_rank], par, r, W, p.Hkv, kvh, pf);
+            lr[r] = __ldcg(src + GD + h);
+            orr[r] = __ldcg(src + idx);
+            mx = fmaxf(mx, lr[r]);
+          }
+        }
+        const float mxu = (mx == -INFINITY) ? 0.0f : mx;
+        float sum = 0.0f, o = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+          if (r < W) {
+            const float w = exp2f(lr[r] - mxu);
+            sum += w;
+            o += w * orr[r];
+          }
+        }
+        write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
+      }
+    }
+    // the last slice merger of this call advances the epoch for the next call
+    if (ctid == 0) {
+      const unsigned prev = atomicAdd(p.cp_done, 1u);
+      if (prev == static_cast<unsigned>(p.cp_mergers) - 1u) {
+        *p.cp_done = 0u;
+        *p.cp_epoch = cp_e;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// log-sum-exp merge of QIC_PARTIAL_OUT partials (one thread per output element)
+// ----------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256) merge_partials_kernel(const float* __restrict__ partials, int n, int H,
+                                                             int Hkv, const T* __restrict__ gate, T* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H * D) return;
+  const int G = H / Hkv, pf = partial_floats(G, D);
+  const int h = i / D, d = i - h * D, kvh = h / G, hh = h - kvh * G;
+  float mx = -INFINITY;
+  for (int k = 0; k < n; ++k) mx = fmaxf(mx, partials[(static_cast<size_t>(k) * Hkv + kvh) * pf + G * D + hh]);
+  const float mxu = (mx == -INFINITY) ? 0.0f : mx;
+  float sum = 0.0f, o = 0.0f;
+  for (int k = 0; k < n; ++k) {
+    const float* pk = partials + (static_cast<size_t>(k) * Hkv + kvh) * pf;
+    const float w = exp2f(pk[G * D + hh] - mxu);
+    sum += w;
+    o += w * pk[hh * D + d];
+  }
+  write_out<T>(out, gate, static_cast<size_t>(i), sum > 0.0f ? o / sum : 0.0f);
+}
+
+template <typename T, int D>
+static cudaError_t launch_merge_typed(const float* partials, int n, int H, int Hkv, const void* gate, void* out,
+                                      cudaStream_t stream) {
+  const int total = H * D;
+  merge_partials_kernel<T, D><<<(total + 255) / 256, 256, 0, stream>>>(partials, n, H, Hkv,
+                                                                     static_cast<const T*>(gate), static_cast<T*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partials, int n, int H, int Hkv,
+                                   const void* gate, void* out, cudaStream_t stream) {
+  if (dtype == QIC_DTYPE_BF16) {
+    switch (head_dim) {
+      case 64: return launch_merge_typed<__nv_bfloat16, 64>(partials, n, H, Hkv, gate, out, stream);
+      case 128: return launch_merge_typed<__nv_bfloat16, 128>(partials, n, H, Hkv, gate, out, stream);
+      case 256: return launch_merge_typed<__nv_bfloat16, 256>(partials, n, H, Hkv, gate, out, stream);
+    }
+  } else {
+    switch (head_dim) {
+      case 64: return launch_merge_typed<__half, 64>(partials, n, H, Hkv, gate, out, stream);
+      case 128: return launch_merge_typed<__half, 128>(partials, n, H, Hkv, gate, out, stream);
+      case 256: return launch_merge_typed<__half, 256>(partials, n, H, Hkv, gate, out, stream);
+    }
+  }
+  return cudaErrorInvalidValue;
 }
 
 // ----------------------------------------------------------------------------

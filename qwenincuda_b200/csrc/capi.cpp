@@ -235,6 +235,7 @@ void fill_common(qic::AttnParams& p, int H, int Hkv, int D, const void* q, const
   p.G = H / Hkv;
   p.head_dim = D;
   p.flags = static_cast<int>(flags & (QIC_FUSE_Q_PROLOGUE | QIC_FUSE_APPEND | QIC_PDL));
+  p.rope_pos = -1;
   p.eps = eps;
   p.theta = theta;
   p.scale_log2 = static_cast<float>((1.0 / std::sqrt(static_cast<double>(D))) * 1.4426950408889634);
@@ -255,7 +256,10 @@ int box_height(bool paged, int page_size, int tok, int* log2) {
 
 }  // namespace
 
-int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
+namespace {
+
+// Single-sequence decode attention; cp != nullptr adds the context-parallel exchange.
+int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_stream_t stream) {
   if (a == nullptr) return QIC_ERROR_INVALID_VALUE;
   const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim, S = a->seq_len;
   int rc = check_attention_common(a->dtype, H, Hkv, D, a->flags, a->q, a->out, a->k_cache, a->v_cache, a->gate,
@@ -277,7 +281,33 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   if (cache_tokens <= 0 || cache_tokens > (int64_t(1) << 31) - 1) return QIC_ERROR_INVALID_VALUE;
   if (!paged && S > cache_tokens) return QIC_ERROR_INVALID_VALUE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool partial_out = (a->flags & QIC_PARTIAL_OUT) != 0;
+  if (partial_out && (cp != nullptr || !aligned16(a->out))) return QIC_ERROR_INVALID_VALUE;
+  if ((a->flags & QIC_EXPLICIT_POSITION) && (a->position < 0 || a->position > INT32_MAX - 1))
+    return QIC_ERROR_INVALID_VALUE;
+  if (cp != nullptr) {
+    if (cp->world < 1 || cp->world > qic::kMaxRanks || cp->rank < 0 || cp->rank >= cp->world ||
+        cp->exchange == nullptr || cp->peer_exchange[cp->rank] != cp->exchange || a->workspace == nullptr ||
+        a->workspace_bytes < qic::kWsPartialOffset || cp->timeout_ms < 0)
+      return QIC_ERROR_INVALID_VALUE;
+    for (int r = 0; r < cp->world; ++r)
+      if (cp->peer_exchange[r] == nullptr || !aligned16(cp->peer_exchange[r])) return QIC_ERROR_INVALID_VALUE;
+    if (cp->exchange_bytes < qic::cp_exchange_bytes(G, D, Hkv, cp->world)) return QIC_ERROR_WORKSPACE;
+    if (a->cluster_size != 0 && a->cluster_size != qic::kCpSlices) return QIC_ERROR_NOT_SUPPORTED;
+    if (a->num_splits != 0 && a->num_splits % qic::kCpSlices != 0) return QIC_ERROR_NOT_SUPPORTED;
+    // every rank must reach the exchange: a shard shorter than one cluster of stages is not supported
+    if (S < qic::kCpSlices * qic::stage_tokens(D)) return QIC_ERROR_NOT_SUPPORTED;
+  }
   if (S == 0) {  // no tokens: the reference writes acc * 1e12 = 0
+    if (partial_out) {  // o = 0 and lse = -inf for every head
+      const int G0 = H / Hkv, pf = qic::partial_floats(G0, D);
+      std::vector<float> host(static_cast<size_t>(Hkv) * pf, 0.0f);
+      for (int k = 0; k < Hkv; ++k)
+        for (int h = 0; h < G0; ++h) host[static_cast<size_t>(k) * pf + G0 * D + h] = -INFINITY;
+      cudaError_t e = cudaMemcpyAsync(a->out, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+      return cuda_status(e);
+    }
     return cuda_status(cudaMemsetAsync(a->out, 0, static_cast<size_t>(H) * D * 2, st));
   }
 
@@ -293,6 +323,7 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   const int n_stages = (S + tok - 1) / tok;
   int n_splits = a->num_splits, cluster = a->cluster_size;
   if (cluster < 0 || cluster > qic::kMaxCluster) return QIC_ERROR_INVALID_VALUE;
+  if (cp != nullptr) cluster = qic::kCpSlices;
   if (n_splits <= 0) {
     // As many CTAs as can be resident in one wave: clusters of 8 (measured best on B200),
     // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
@@ -314,6 +345,7 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
     n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
     cluster = n_splits;
   }
+  if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0)) return QIC_ERROR_NOT_SUPPORTED;
   const int n_clusters = n_splits / cluster;
   if (n_clusters > 1) {
     const size_t need = qic::kWsPartialOffset +
@@ -342,7 +374,94 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   p.log2_box_h = lbh;
   p.n_stages = n_stages;
   p.n_splits = n_splits;
+  p.rope_pos = (a->flags & QIC_EXPLICIT_POSITION) ? a->position : -1;
+  if (partial_out) p.part_out = static_cast<float*>(a->out);
+  if (cp != nullptr) {
+    char* ws = static_cast<char*>(a->workspace);
+    p.cp_rank = cp->rank;
+    p.cp_world = cp->world;
+    p.cp_mergers = Hkv * cluster;
+    p.cp_epoch = reinterpret_cast<unsigned*>(ws + qic::kWsCpEpoch);
+    p.cp_done = reinterpret_cast<unsigned*>(ws + qic::kWsCpDone);
+    for (int r = 0; r < cp->world; ++r) p.cp_peer[r] = cp->peer_exchange[r];
+    if (cp->timeout_ms > 0) p.timeout_ns = static_cast<uint64_t>(cp->timeout_ms) * 1000000ull;
+  }
   return cuda_status(qic::launch_decode_attention(a->dtype, D, p, st));
+}
+
+}  // namespace
+
+int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
+  return decode_attention_impl(a, nullptr, stream);
+}
+
+int qic_cp_decode_attention(const qic_decode_args* a, const qic_cp_args* cp, qic_stream_t stream) {
+  if (cp == nullptr) return QIC_ERROR_INVALID_VALUE;
+  return decode_attention_impl(a, cp, stream);
+}
+
+size_t qic_cp_exchange_bytes(int num_heads, int num_kv_heads, int head_dim, int world) {
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || head_dim <= 0 || world < 1 ||
+      world > qic::kMaxRanks)
+    return 0;
+  return qic::cp_exchange_bytes(num_heads / num_kv_heads, head_dim, num_kv_heads, world);
+}
+
+size_t qic_partial_floats(int num_heads, int num_kv_heads, int head_dim) {
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(qic::partial_floats(num_heads / num_kv_heads, head_dim));
+}
+
+int qic_attention_merge(int dtype, const float* partials, int num_partials, int num_heads, int num_kv_heads,
+                        int head_dim, const void* gate, void* out, qic_stream_t stream) {
+  if (!valid_dtype(dtype) || partials == nullptr || out == nullptr || num_partials < 1 || num_heads <= 0 ||
+      num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+    return QIC_ERROR_INVALID_VALUE;
+  if (!supported_head_dim(head_dim) || num_heads / num_kv_heads > qic::kMaxGroup) return QIC_ERROR_NOT_SUPPORTED;
+  if (!aligned2(out) || (gate && !aligned2(gate)) || (reinterpret_cast<uintptr_t>(partials) & 3u))
+    return QIC_ERROR_MISALIGNED;
+  return cuda_status(qic::launch_attention_merge(dtype, head_dim, partials, num_partials, num_heads, num_kv_heads, gate,
+                                                 out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qic_device_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return QIC_ERROR_INVALID_VALUE;
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess && *ptr != nullptr) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+  }
+  return cuda_status(e);
+}
+
+int qic_device_free(void* ptr) { return ptr == nullptr ? QIC_SUCCESS : cuda_status(cudaFree(ptr)); }
+
+int qic_ipc_get_handle(const void* ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) <= QIC_IPC_HANDLE_BYTES, "IPC handle size");
+  if (ptr == nullptr || handle == nullptr) return QIC_ERROR_INVALID_VALUE;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_status(e);
+  std::memset(handle, 0, QIC_IPC_HANDLE_BYTES);
+  std::memcpy(handle, &h, sizeof(h));
+  return QIC_SUCCESS;
+}
+
+int qic_ipc_open_handle(const void* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return QIC_ERROR_INVALID_VALUE;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return QIC_ERROR_PEER;
+  return QIC_SUCCESS;
+}
+
+int qic_ipc_close_handle(void* ptr) {
+  if (ptr == nullptr) return QIC_ERROR_INVALID_VALUE;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? QIC_SUCCESS : QIC_ERROR_PEER;
 }
 
 int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv_heads, int head_dim,

@@ -28,8 +28,24 @@ constexpr size_t kWsPartialOffset = kWsHeader + static_cast<size_t>(kMaxCounters
 // (32 / 16 tokens) and 8 KB for head_dim 64 (32 tokens).
 __host__ __device__ constexpr int stage_tokens(int head_dim) { return head_dim > 128 ? 16 : 32; }
 
-// One partial of a (kv head, split): lse[G] (log2 domain) then o[G][D] (normalised), fp32.
+// One partial of a (kv head, split): o[G][D] (normalised) then lse[G] (log2 domain),
+// fp32, padded to a multiple of 4 floats.
 __host__ __device__ constexpr int partial_floats(int G, int D) { return ((G * (D + 1)) + 3) & ~3; }
+
+// Context parallelism. Workspace header words: calls completed (the exchange epoch)
+// at byte 64, slice mergers finished in the current call at byte 128.
+constexpr size_t kWsCpEpoch = 64;
+constexpr size_t kWsCpDone = 128;
+constexpr int kMaxRanks = QIC_MAX_RANKS;
+constexpr int kCpSlices = 8;  // exchange slices per kv head: one per CTA of an 8-CTA cluster
+// Exchange buffer of one rank: flags [2][world][Hkv][kCpSlices] u32 (the epoch that
+// last published that slice; parity = epoch & 1), then data [2][world][Hkv][partial].
+__host__ __device__ constexpr size_t cp_flags_bytes(int Hkv, int world) {
+  return (static_cast<size_t>(2) * world * Hkv * kCpSlices * 4 + 255) & ~static_cast<size_t>(255);
+}
+__host__ __device__ constexpr size_t cp_exchange_bytes(int G, int D, int Hkv, int world) {
+  return cp_flags_bytes(Hkv, world) + static_cast<size_t>(2) * world * Hkv * partial_floats(G, D) * 4;
+}
 
 // Work of one CTA in a planned (batched) launch: stages [st_lo, st_hi) of sequence b
 // for kv head kvh, being split `split` of `nsplit` for that (b, kvh); its partial goes
@@ -72,11 +88,22 @@ struct AttnParams {
   int flags;
   float eps, theta, scale_log2;
   uint64_t timeout_ns;
+  long long rope_pos;                // RoPE position of q and the appended k (single-sequence launches)
+  float* part_out;                   // QIC_PARTIAL_OUT: [Hkv][partial_floats] instead of out
+  // context parallelism (cp_world == 0: off)
+  int cp_rank, cp_world;
+  int cp_mergers;                    // slice mergers per call on this rank: Hkv * cluster
+  unsigned* cp_epoch;                // workspace words kWsCpEpoch / kWsCpDone
+  unsigned* cp_done;
+  void* cp_peer[kMaxRanks];          // every rank's exchange buffer, addressable here
 };
 
 // Launchers (attn_kernel.cu)
 cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream);
 size_t decode_attention_smem_bytes(int head_dim);
+// out = log-sum-exp merge of n partials [n][Hkv][partial_floats] (+ gate)
+cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partials, int n, int H, int Hkv,
+                                   const void* gate, void* out, cudaStream_t stream);
 // Clusters of `cluster` CTAs of the decode kernel that can be resident at once (0 if unknown).
 int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster);
 

@@ -16,8 +16,10 @@ import torch
 from .abi import (
     QIC_DTYPE_BF16,
     QIC_DTYPE_F16,
+    QIC_EXPLICIT_POSITION,
     QIC_FUSE_APPEND,
     QIC_FUSE_Q_PROLOGUE,
+    QIC_PARTIAL_OUT,
     QIC_PDL,
     QIC_PLAN_ITEM_BYTES,
     BatchDecodeArgs,
@@ -103,7 +105,10 @@ def kv_append(k_new, v_new, k_norm_w, eps, rope_theta, position, k_cache, v_cach
 def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, seq_len, page_table=None,
                 page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
                 rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
-                cache_tokens=None, pdl=False, cluster_size=0) -> DecodeArgs:
+                cache_tokens=None, pdl=False, cluster_size=0, position=None, partial_out=False) -> DecodeArgs:
+    """qic_decode_args for one call. position: RoPE position of q and the appended k
+    (default seq_len - 1). partial_out: `out` is an fp32 tensor of
+    num_kv_heads * partial_floats(...) elements receiving the (o, lse) partial."""
     a = DecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads = num_heads
@@ -119,6 +124,13 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
     a.gate = _ptr(gate)
     a.out = _ptr(out)
     a.flags = _flags(fuse_q, fuse_append, pdl)
+    if position is not None:
+        a.flags |= QIC_EXPLICIT_POSITION
+        a.position = int(position)
+    if partial_out:
+        if out.dtype != torch.float32:
+            raise TypeError("a partial output is float32")
+        a.flags |= QIC_PARTIAL_OUT
     a.eps = eps
     a.rope_theta = rope_theta
     a.q_norm_w = _ptr(q_norm_w)
@@ -141,6 +153,20 @@ def decode_attention(stream=None, **kw):
     """Split-KV decode attention; see qic_decode_attention in include/qic.h."""
     a = decode_args(**kw)
     check(lib().qic_decode_attention(ctypes.byref(a), _stream(stream)), "qic_decode_attention")
+
+
+def partial_floats(num_heads: int, num_kv_heads: int, head_dim: int) -> int:
+    """fp32 elements per kv head of a partial: G*d outputs, G log-sum-exp values, padding."""
+    return int(lib().qic_partial_floats(num_heads, num_kv_heads, head_dim))
+
+
+def attention_merge(partials, num_heads, num_kv_heads, head_dim, out, gate=None, stream=None):
+    """out = log-sum-exp merge of stacked partials [n, Hkv, partial_floats] (+ gate)."""
+    if partials.dtype != torch.float32:
+        raise TypeError("partials are float32")
+    n = partials.numel() // (num_kv_heads * partial_floats(num_heads, num_kv_heads, head_dim))
+    check(lib().qic_attention_merge(dtype_code(out), _ptr(partials), n, num_heads, num_kv_heads, head_dim, _ptr(gate),
+                                    _ptr(out), _stream(stream)), "qic_attention_merge")
 
 
 def launch_flash_attention(q, k_cache, v_cache, num_heads, num_kv_heads, head_dim, seq_len, context,
