@@ -10,9 +10,15 @@ dependent launch inside a CUDA graph. Synthetic seeded data; the step's K/V (1.2
 is larger than L2. The contiguous (flash) layout is timed as well.
 
 metric: decode-attn KV-read GB/s = (K+V bytes read for S tokens + append bytes) per
-layer x layers / step time; also reported as us per layer. N > 1 GPUs run one
-independent replica per GPU (this path has no collective): value = total bytes / the
-slowest rank's step time.
+layer x layers / step time; also reported as us per layer. N > 1 GPUs (torchrun, one
+process per GPU): the default workload runs one independent replica per GPU (a
+single-sequence layer does not shard; weak scaling, value = N x bytes / the slowest
+rank's step time), and the same JSON line carries the partitioned configurations at
+that N: the 131073-token sequence split across the ranks with the fused in-kernel
+NVLink exchange (and the NCCL all-gather path timed beside it), and the 64-sequence
+batch partitioned by K/V bytes (strong scaling: total bytes / the slowest rank's
+time). --workload qwen3_8b_s131073 or qwen3_8b_batch64 with N > 1 makes those the
+line's value.
 
 Other workloads (--workload): qwen3_0p6b_s1025, qwen35_gated_s32769 (d=256 with the
 output gate), qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step;
@@ -297,11 +303,19 @@ def pair_workload():
 
 
 def batched_workload(world, rank):
+    """64 sequences; with N ranks each decodes its share (partition_sequences: balanced
+    by K/V bytes) from its own page pool of about 1.1M/N tokens; no exchange."""
+    import dataclasses
+
     import qwenincuda_b200 as q
+    from qwenincuda_b200.context_parallel import partition_sequences
     from qwenincuda_b200.workloads import BatchConfig, batched_bytes, make_batched_inputs
 
     cfg = BatchConfig()
-    lens = cfg.seq_lens()
+    all_lens = cfg.seq_lens()
+    mine = partition_sequences(all_lens, world)[rank]
+    lens = [all_lens[i] for i in mine]
+    cfg = dataclasses.replace(cfg, pool_tokens=(cfg.pool_tokens + world - 1) // world, seed=cfg.seed + 101 * rank)
     inp = make_batched_inputs(cfg, seq_lens=lens)
     plan = q.BatchPlan(lens, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
     a = q.ops.batch_decode_args(plan=plan, q=inp["q"], k_cache=inp["k_cache"], v_cache=inp["v_cache"],
@@ -323,13 +337,144 @@ def batched_workload(world, rank):
         ho.copy_(inp["out"], non_blocking=True)
 
     nbytes = batched_bytes(lens, cfg.kv_dim)
-    return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes,
+    return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes, partitioned=world > 1,
                 e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2), kernel="decode_attn_kernel",
                 status=plan.status, keep=(inp, plan, a),
-                config={"batch": cfg.batch, "seq_lens": f"U[{cfg.min_len},{cfg.max_len}]+1, seed {cfg.seed}",
-                        "tokens": sum(lens), "page_size": cfg.page_size, "pool_tokens": inp["cache_tokens"],
+                config={"batch": cfg.batch, "seq_lens": f"U[{cfg.min_len},{cfg.max_len}]+1, seed {BatchConfig().seed}",
+                        "sequences_on_rank0": len(lens) if rank == 0 else None, "ranks": world,
+                        "tokens_total": sum(all_lens), "page_size": cfg.page_size, "pool_tokens_per_rank": inp["cache_tokens"],
                         "plan_items": plan.items, "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads,
                         "head_dim": cfg.head_dim})
+
+
+def cp_workload(world, rank, with_allgather=True):
+    """One 131073-token sequence (Qwen3-8B attention shape, page 16, shuffled tables)
+    split into N contiguous page ranges, one per rank (shard_tokens). A step is one
+    fused qic_cp_decode_attention per rank: q prologue at the global position, the
+    append on the rank that holds the last token, attention over the rank's shard,
+    and the in-kernel NVLink exchange + log-sum-exp merge of the ranks' partials.
+    Each rank's shard is seeded independently; q, k_new and v_new are the same on
+    every rank."""
+    import qwenincuda_b200 as q
+    from qwenincuda_b200 import context_parallel as cpm
+    from qwenincuda_b200.workloads import CONFIGS
+
+    cfg = CONFIGS["qwen3_8b_s131073"]
+    H, Hkv, d, S, P = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len, cfg.page_size
+    t0, t1 = cpm.shard_tokens(S, P, world)[rank]
+    n = t1 - t0
+    pages = (n + P - 1) // P
+    dtype = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(cfg.seed * 1000 + 17 * rank + 1)
+    kc = (torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype)
+    vc = (torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype)
+    table = torch.randperm(pages, generator=g, device="cuda").to(torch.int32)
+    gs = torch.Generator(device="cuda").manual_seed(cfg.seed * 1000 + 999)
+    qv = torch.randn(H * d, generator=gs, device="cuda").to(dtype)
+    kn = torch.randn(Hkv * d, generator=gs, device="cuda").to(dtype)
+    vn = (torch.randn(Hkv * d, generator=gs, device="cuda") * cfg.kv_std).to(dtype)
+    ones = torch.ones(d, device="cuda", dtype=dtype)
+    out = torch.zeros(H * d, device="cuda", dtype=dtype)
+    ws = q.Workspace(H, Hkv, d, n)
+    owner = rank == world - 1
+    group = cpm.ExchangeGroup(H, Hkv, d, rank, world)
+    kw = dict(q=qv, k_cache=kc, v_cache=vc, num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=n, page_table=table,
+              page_size=P, q_norm_w=ones, k_norm_w=ones, k_new=kn, v_new=vn, eps=cfg.eps, rope_theta=cfg.rope_theta,
+              fuse_q=True, fuse_append=owner, workspace=ws, cache_tokens=pages * P, position=S - 1)
+    a = q.ops.decode_args(out=out, **kw)
+    lib = q.lib()
+    cp_ptr = ctypes.byref(group.args)
+
+    def step():
+        rc = lib.qic_cp_decode_attention(ctypes.byref(a), cp_ptr, torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise q.QicError(rc, "qic_cp_decode_attention")
+
+    hq, hk, hv = qv.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    ho = torch.empty_like(out, device="cpu").pin_memory()
+
+    def e2e():
+        qv.copy_(hq, non_blocking=True)
+        kn.copy_(hk, non_blocking=True)
+        vn.copy_(hv, non_blocking=True)
+        step()
+        ho.copy_(out, non_blocking=True)
+
+    nbytes = 2 * n * Hkv * d * 2 + (2 * Hkv * d * 2 if owner else 0)
+    allgather = None
+    if with_allgather and world > 1:
+        import torch.distributed as dist
+
+        pf = q.ops.partial_floats(H, Hkv, d)
+        part = torch.empty(Hkv * pf, device="cuda", dtype=torch.float32)
+        gathered = torch.empty(world * Hkv * pf, device="cuda", dtype=torch.float32)
+        out2 = torch.zeros_like(out)
+        ws2 = q.Workspace(H, Hkv, d, n)
+        kw2 = dict(kw, workspace=ws2, fuse_append=False)
+        a2 = q.ops.decode_args(out=part, partial_out=True, **kw2)
+
+        def ag_step():
+            rc = lib.qic_decode_attention(ctypes.byref(a2), torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise q.QicError(rc, "qic_decode_attention")
+            dist.all_gather_into_tensor(gathered, part)
+            q.ops.attention_merge(gathered, H, Hkv, d, out2)
+
+        allgather = ag_step
+    return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes, partitioned=True,
+                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2),
+                kernel="decode_attn_kernel (fused NVLink exchange)", status=ws.status, allgather=allgather,
+                keep=(kc, vc, table, qv, kn, vn, out, ws, group, a),
+                config={"seq_len": S, "page_size": P, "num_heads": H, "num_kv_heads": Hkv, "head_dim": d,
+                        "ranks": world, "shard_tokens_rank0": cpm.shard_tokens(S, P, world)[0][1],
+                        "exchange": "in-kernel NVLink stores + system-scope flags, log-sum-exp merge"})
+
+
+def time_eager(fn, steps, warmup, world):
+    """ms per call of fn (no graph): used for the NCCL all-gather path."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(s.elapsed_time(e) / steps, world)
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def partitioned_summary(wl, args, world, local, peaks):
+    """Measures a partitioned workload (every rank its own share) and returns the
+    whole-job numbers: total algorithmic bytes of all ranks / the slowest rank's time."""
+    ms, ms_e2e, clocks = measure(wl, args, world, local)
+    total = sum_over_ranks(float(wl["bytes"]), world)
+    per_rank_gbs = wl["bytes"] / (ms * 1e-3) / 1e9
+    res = {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+           "us_per_step": round(ms * 1000, 2), "bytes_total": int(total),
+           "e2e": {"value": round(total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                   "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2]},
+           "rank0_frac_of_hbm": round(per_rank_gbs / peaks["hbm_gbs"], 4), "scaling": "strong",
+           "config": wl["config"]}
+    if wl.get("allgather") is not None:
+        ms_ag = time_eager(wl["allgather"], args.steps, args.warmup, world)
+        res["allgather_nccl_path"] = {"value": round(total / (ms_ag * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                      "us_per_step": round(ms_ag * 1000, 2),
+                                      "what": "partial kernel + NCCL all_gather_into_tensor + merge kernel"}
+    return res, ms, ms_e2e, clocks
 
 
 def measure(wl, args, world, local):
@@ -473,7 +618,14 @@ def main():
 
     peaks = load_peaks()
     extra = {}
-    if args.workload in ATTN_WORKLOADS:
+    partitioned_mode = world > 1 and args.workload in ("qwen3_8b_s131073", "qwen3_8b_batch64")
+    if args.workload == "qwen3_8b_s131073" and world > 1:
+        # the long sequence split across the ranks, partials exchanged in-kernel
+        wl = cp_workload(world, rank)
+        res, ms, ms_e2e, clocks = partitioned_summary(wl, args, world, local, peaks)
+        if "allgather_nccl_path" in res:
+            extra["allgather_nccl_path"] = res["allgather_nccl_path"]
+    elif args.workload in ATTN_WORKLOADS:
         wl = attention_workload(args.workload, "paged", args.layers)
         ms, ms_e2e, clocks = measure(wl, args, world, local)
         wl_c = attention_workload(args.workload, "contiguous", args.layers)
@@ -494,27 +646,46 @@ def main():
         raise SystemExit(f"unknown workload {args.workload}")
 
     step_bytes = wl["bytes"]
-    value = world * step_bytes / (ms * 1e-3) / 1e9
+    if partitioned_mode:
+        # every rank processed its own share: whole-job bytes / the slowest rank's time
+        total_bytes = sum_over_ranks(float(step_bytes), world)
+        scaling = "strong"
+        parallelism = (f"context-parallel{world}" if args.workload == "qwen3_8b_s131073"
+                       else f"partitioned{world}")
+    else:
+        total_bytes = float(world * step_bytes)
+        scaling = "weak"
+        parallelism = f"replicas{world}" if world > 1 else "single"
+    value = total_bytes / (ms * 1e-3) / 1e9
     per_launch_ms = ms / wl["launches"]
     achieved = wl["bytes_per_launch"] / (per_launch_ms * 1e-3) / 1e9
-    traffic = measured_traffic(args.workload)
+    traffic = measured_traffic(args.workload) if world == 1 else None
+    if world > 1 and args.workload == "qwen3_8b_s8192":
+        # the partitioned configurations at the same N (one JSON line per run)
+        wl_cp = cp_workload(world, rank)
+        extra["context_parallel_qwen3_8b_s131073"] = partitioned_summary(wl_cp, args, world, local, peaks)[0]
+        del wl_cp
+        wl_b = batched_workload(world, rank)
+        extra["partitioned_qwen3_8b_batch64"] = partitioned_summary(wl_b, args, world, local, peaks)[0]
+        del wl_b
     line = {
         "metric": "decode-attn KV-read GB/s" if args.workload != "qwen35_gdn" else "GatedDeltaNet state GB/s",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "us_per_layer": round(per_launch_ms * 1000, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": dict(workload=args.workload, parallelism=f"replicas{world}" if world > 1 else "single",
-                       l2="step inputs larger than the 126 MB L2" if step_bytes > (126 << 20)
+        "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": dict(workload=args.workload, parallelism=parallelism,
+                       l2="step inputs larger than the 126 MB L2" if total_bytes > (126 << 20)
                        else "step smaller than L2; consecutive steps re-read it",
                        **wl["config"]),
         **extra,
-        "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "e2e": {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2],
                 "ms_per_step": round(ms_e2e, 4)},
         "roofline": {"bound": "hbm", "kernel": wl["kernel"], "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                      "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"],
-                     "launch_time": "step time / launches per step (includes launch gaps)",
+                     "launch_time": "step time / launches per step (includes launch gaps)"
+                     + ("; rank 0's bytes over the slowest rank's time" if partitioned_mode else ""),
                      "traffic": traffic},
         "gpu_launches": wl["launches"] * args.steps,
         "clocks": clocks,
@@ -528,6 +699,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank unmaps an exchange buffer a peer may still write
         dist.destroy_process_group()
 
 
