@@ -210,12 +210,14 @@ typedef struct qic_cp_args {
 /* Bytes of one rank's exchange buffer. */
 size_t qic_cp_exchange_bytes(int num_heads, int num_kv_heads, int head_dim, int world);
 
-/* Decode attention of one shard of a sequence, fused with the exchange: the CTA that
- * holds a slice of this rank's merged partial stores it into every rank's exchange
- * buffer over NVLink and raises a flag there, waits (bounded) for the same slice from
- * every other rank, merges the world partials by log-sum-exp and writes out (with the
- * gate). Every rank calls it once per step with the same shapes, cluster size (8)
- * and number of calls; args->workspace is required (it keeps the call epoch).
+/* Decode attention of one shard of a sequence, fused with the exchange: every
+ * 8-CTA cluster stores its merged (o, lse) slices into every rank's exchange buffer
+ * over NVLink as 8-byte words {value, call tag} (one store each: no fence or flag),
+ * and one CTA per (kv head, slice) on each rank polls the words of every (rank,
+ * cluster) contribution (bounded wait), merges them by log-sum-exp and writes out
+ * (with the gate). At most 16 clusters per kv head on a rank. Every rank calls it
+ * once per step with the same shapes, cluster size (8) and number of calls;
+ * args->workspace is required (it keeps the call epoch).
  * Shard layout: each rank's args describe its own tokens (seq_len, page_table or
  * contiguous rows); q is the same on every rank; QIC_EXPLICIT_POSITION gives the
  * global position for RoPE; the rank holding the last token sets QIC_FUSE_APPEND.
@@ -272,8 +274,9 @@ typedef struct qic_batch_decode_args {
 /* Host-side planner. seq_lens[b] (host memory) is the number of tokens sequence b
  * attends (position+1 when appending). Cuts every (sequence, kv head) into work items of
  * at most ~total/(target_ctas) pipeline stages, ordered longest first, and writes them to
- * `plan` (host memory, max_items * QIC_PLAN_ITEM_BYTES bytes). target_ctas 0 picks
- * 16 x the SM count. Returns the item count and the workspace size the plan needs. */
+ * `plan` (host memory, max_items * QIC_PLAN_ITEM_BYTES bytes). target_ctas 0 picks whole
+ * waves of the CTAs the GPU holds at once, with about 1 MiB or more of K/V per item and
+ * at most 16 items per SM. Returns the item count and the workspace size the plan needs. */
 int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
                    int target_ctas, void* plan, int max_items, int* items, size_t* workspace_bytes);
 

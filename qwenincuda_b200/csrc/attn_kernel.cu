@@ -104,14 +104,12 @@ __device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, float o)
   ob[i] = ot;
 }
 
-// Slot of the exchange buffer at `base` for (parity, source rank, kv head): flag of
-// slice c, and the partial [o: G*D][lse: G].
-__device__ __forceinline__ unsigned* cp_flag(void* base, int par, int src, int world, int Hkv, int kvh, int c) {
-  return static_cast<unsigned*>(base) + ((static_cast<size_t>(par) * world + src) * Hkv + kvh) * kCpSlices + c;
-}
-__device__ __forceinline__ float* cp_data(void* base, int par, int src, int world, int Hkv, int kvh, int pf) {
-  return reinterpret_cast<float*>(static_cast<char*>(base) + cp_flags_bytes(Hkv, world)) +
-         ((static_cast<size_t>(par) * world + src) * Hkv + kvh) * pf;
+// Contribution (parity, source rank, cluster k, kv head, slice c) in the exchange
+// buffer at `base`: cp_slice_words 8-byte words.
+__device__ __forceinline__ uint2* cp_slot(void* base, int par, int src, int k, int world, int Hkv, int kvh, int c,
+                                          int words) {
+  const size_t i = ((((static_cast<size_t>(par) * world + src) * kCpMaxClusters + k) * Hkv + kvh) * kCpSlices + c);
+  return static_cast<uint2*>(base) + i * words;
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -530,19 +528,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const bool cp = p.cp_world > 0;
   unsigned cp_e = 0;  // exchange epoch of this call (slice mergers, context parallel)
   // Destination of the final value o of output idx (head h, log-sum-exp lse): the
-  // output, the caller's fp32 partial (QIC_PARTIAL_OUT), or the slot of this rank in
-  // every rank's exchange buffer.
+  // output or the caller's fp32 partial (QIC_PARTIAL_OUT).
   auto emit = [&](int idx, int h, float o, float lse, bool head_first) {
     if (p.part_out != nullptr) {
       float* po = p.part_out + static_cast<size_t>(kvh) * pf;
       po[idx] = o;
       if (head_first) po[GD + h] = lse;
-    } else if (cp) {
-      for (int r = 0; r < p.cp_world; ++r) {
-        float* dst = cp_data(p.cp_peer[r], cp_e & 1, p.cp_rank, p.cp_world, p.Hkv, kvh, pf);
-        dst[idx] = o;
-        if (head_first) dst[GD + h] = lse;
-      }
     } else {
       write_out<T>(ob, gb, qoff + idx, o);
     }
@@ -572,7 +563,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
-  if (cp && nclust == 1) cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
+  // context parallel: this cluster's slice goes to every rank as one contribution
+  const int cpw = cp_slice_words(G, D);
+  unsigned cp_tag = 0;
+  if (cp) {
+    cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
+    cp_tag = ((cp_e & 0xffffffu) << 8) | static_cast<unsigned>(nclust);
+  }
   float* gslot = p.part + static_cast<size_t>(part_base + cid) * pf;  // [o: G*D][lse: G]
 #pragma unroll 1
   for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
@@ -601,7 +598,15 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
     o = sum > 0.0f ? o / sum : 0.0f;
-    if (nclust == 1) {
+    if (cp) {
+      const float lse = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
+      for (int r = 0; r < p.cp_world; ++r) {
+        uint2* slot = cp_slot(p.cp_peer[r], cp_e & 1, p.cp_rank, cid, p.cp_world, p.Hkv, kvh, rank, cpw);
+        st_word_sys(slot + (idx - lo), o, cp_tag);
+        if (idx == lo) st_word_sys(slot + cpw - 2, lse, cp_tag);
+        if (idx == hi - 1) st_word_sys(slot + cpw - 1, lse, cp_tag);
+      }
+    } else if (nclust == 1) {
       emit(idx, h, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY, idx == lo || idx - h * D == 0);
     } else {
       gslot[idx] = o;
@@ -610,7 +615,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   }
   // every CTA of the cluster has read the partials it needs from this one
   cluster_sync_all();
-  if (nclust > 1) {
+  if (nclust > 1 && !cp) {
     // ---- merge the cluster partials of this slice: last arriving cluster ----
     consumer_sync();
     const int counter = (b * p.Hkv + kvh) * C + rank;
@@ -620,7 +625,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     consumer_sync();
     if (flags_s[1]) {
-      if (cp) cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
       const float* g0 = p.part + static_cast<size_t>(part_base) * pf;
 #pragma unroll 1
       for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
@@ -652,65 +656,107 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       if (ctid == 0) p.counters[counter] = 0;  // ready for the next call
     }
   }
-  if (cp && (nclust == 1 || flags_s[1] != 0)) {
-    // ---- context parallel: publish this slice to every rank, wait for theirs, merge ----
-    // The cluster has 8 CTAs (kCpSlices) on every rank, so slice `rank` covers the same
-    // outputs [lo, hi) everywhere.
+  if (cp && cid == 0) {
+    // ---- context parallel: CTA `rank` of cluster 0 merges slice `rank` of this kv
+    // head from every (rank, cluster) contribution, polling the tagged words ----
     const int W = p.cp_world, par = cp_e & 1;
-    if (ctid == 0) flags_s[2] = 0;
-    consumer_sync();  // every thread's stores of this slice are issued
-    if (ctid == 0) {
-      fence_acq_rel_sys();
-      for (int r = 0; r < W; ++r) st_relaxed_sys_u32(cp_flag(p.cp_peer[r], par, p.cp_rank, W, p.Hkv, kvh, rank), cp_e);
-    }
-    if (ctid < W) {
-      const unsigned* f = cp_flag(p.cp_peer[p.cp_rank], par, ctid, W, p.Hkv, kvh, rank);
-      const uint64_t dl = globaltimer_ns() + p.timeout_ns;
-      bool ok = false;
+    const unsigned want = cp_e & 0xffffffu;
+    const uint64_t dl = globaltimer_ns() + p.timeout_ns;
+    bool late = false;
 #pragma unroll 1
-      for (uint32_t it = 0;; ++it) {
-        if (ld_acquire_sys_u32(f) == cp_e) {
-          ok = true;
-          break;
-        }
-        if ((it & 15u) == 0 && globaltimer_ns() > dl) break;
-        __nanosleep(64);
-      }
-      if (!ok) {
-        record_status(p.status, QIC_DEV_PEER_TIMEOUT);
-        flags_s[2] = 1;
-      }
-    }
-    consumer_sync();
-    if (flags_s[2] == 0 && !aborted) {
-#pragma unroll 1
-      for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
-        const int h = idx / D;
-        float lr[kMaxRanks], orr[kMaxRanks];
-        float mx = -INFINITY;
+    for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
+      const int h = idx / D;
+      const int lw = (h == lo / D) ? cpw - 2 : cpw - 1;  // log-sum-exp word of this output's head
+      float mx = -INFINITY, sum = 0.0f, o = 0.0f;
+      auto fold = [&](uint2 wo, uint2 wl) {
+        const float lk = __uint_as_float(wl.x), ov = __uint_as_float(wo.x);
+        const float mn = fmaxf(mx, lk);
+        if (mn == -INFINITY) return;
+        const float sc = exp2f(mx - mn), w = exp2f(lk - mn);
+        sum = sum * sc + w;
+        o = o * sc + w * ov;
+        mx = mn;
+      };
+      // Contributions are read kBatch at a time, all loads of a batch in flight
+      // together; a batch is re-read until every tag is this call's. The first
+      // batch is the cluster-0 contribution of every rank, whose tag also gives that
+      // rank's cluster count; then the remaining (rank, cluster) pairs in order.
+      constexpr int kBatch = kMaxRanks;
+      int ncl[kMaxRanks];
+      bool ok = true;
+      int total = 0;
+      for (int j0 = 0; ok; j0 += kBatch) {
+        // pair j: j < W is (rank j, cluster 0); after that, (r, k >= 1) rank-major
+        int rr[kBatch], kk[kBatch];
+        int nb = 0;
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) {
-          if (r < W) {
-            const float* src = cp_data(p.cp_peer[p.cp_rank], par, r, W, p.Hkv, kvh, pf);
-            lr[r] = __ldcg(src + GD + h);
-            orr[r] = __ldcg(src + idx);
-            mx = fmaxf(mx, lr[r]);
+        for (int u = 0; u < kBatch; ++u) {
+          const int j = j0 + u;
+          rr[u] = -1;
+          kk[u] = 0;
+          if (j0 == 0) {
+            if (j < W) {
+              rr[u] = j;
+              nb = u + 1;
+            }
+          } else if (j - W < total) {
+            int rest = j - W, r = 0;
+            while (r < W && rest >= ncl[r] - 1) {
+              rest -= ncl[r] - 1;
+              ++r;
+            }
+            rr[u] = r;
+            kk[u] = rest + 1;
+            nb = u + 1;
           }
         }
-        const float mxu = (mx == -INFINITY) ? 0.0f : mx;
-        float sum = 0.0f, o = 0.0f;
+        if (nb == 0) break;
+        uint2 wo[kBatch], wl[kBatch];
+        unsigned have = 0;  // bit u: pair u holds this call's words
+#pragma unroll 1
+        for (uint32_t it = 0;; ++it) {
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) {
-          if (r < W) {
-            const float w = exp2f(lr[r] - mxu);
-            sum += w;
-            o += w * orr[r];
+          for (int u = 0; u < kBatch; ++u) {
+            if (u < nb && !(have & (1u << u))) {
+              const uint2* slot = cp_slot(p.cp_peer[p.cp_rank], par, rr[u], kk[u], W, p.Hkv, kvh, rank, cpw);
+              wo[u] = ld_word_sys(slot + (idx - lo));
+              wl[u] = ld_word_sys(slot + lw);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u)
+            if (u < nb && (wo[u].y >> 8) == want && (wl[u].y >> 8) == want) have |= 1u << u;
+          if (have == (1u << nb) - 1u) break;
+          if ((it & 15u) == 15u && globaltimer_ns() > dl) {
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (u < nb) {
+            fold(wo[u], wl[u]);
+            if (j0 == 0) ncl[u] = min(static_cast<int>(wo[u].y & 0xffu), kCpMaxClusters);
           }
         }
+        if (j0 == 0) {
+          total = 0;
+          for (int r = 0; r < W; ++r) total += max(ncl[r], 1) - 1;
+          // the (r, k >= 1) pairs start at j = W: continue from there
+          j0 = W - kBatch;
+        }
+      }
+      if (ok && !aborted) {
         write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
+      } else if (!ok) {
+        late = true;
       }
     }
+    if (late) record_status(p.status, QIC_DEV_PEER_TIMEOUT);
     // the last slice merger of this call advances the epoch for the next call
+    consumer_sync();
     if (ctid == 0) {
       const unsigned prev = atomicAdd(p.cp_done, 1u);
       if (prev == static_cast<unsigned>(p.cp_mergers) - 1u) {

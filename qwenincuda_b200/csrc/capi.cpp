@@ -331,6 +331,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     int nclust = std::max(1, max_clusters / Hkv);
+    if (cp != nullptr) nclust = std::min(nclust, qic::kCpMaxClusters);
     n_splits = cluster * nclust;
     if (n_splits > n_stages) {
       nclust = std::max(1, n_stages / cluster);
@@ -345,7 +346,9 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
     cluster = n_splits;
   }
-  if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0)) return QIC_ERROR_NOT_SUPPORTED;
+  if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0 ||
+                        n_splits / qic::kCpSlices > qic::kCpMaxClusters))
+    return QIC_ERROR_NOT_SUPPORTED;
   const int n_clusters = n_splits / cluster;
   if (n_clusters > 1) {
     const size_t need = qic::kWsPartialOffset +
@@ -380,7 +383,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     char* ws = static_cast<char*>(a->workspace);
     p.cp_rank = cp->rank;
     p.cp_world = cp->world;
-    p.cp_mergers = Hkv * cluster;
+    p.cp_mergers = Hkv * qic::kCpSlices;
     p.cp_epoch = reinterpret_cast<unsigned*>(ws + qic::kWsCpEpoch);
     p.cp_done = reinterpret_cast<unsigned*>(ws + qic::kWsCpDone);
     for (int r = 0; r < cp->world; ++r) p.cp_peer[r] = cp->peer_exchange[r];
@@ -476,7 +479,17 @@ int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv
     if (seq_lens[b] < 1) return QIC_ERROR_INVALID_VALUE;
     total += static_cast<long long>((seq_lens[b] + tok - 1) / tok) * num_kv_heads;
   }
-  if (target_ctas <= 0) target_ctas = 16 * sm_count();
+  if (target_ctas <= 0) {
+    // Whole waves of resident CTAs with at least ~1 MiB of K/V per work item (a CTA's
+    // set-up and merge cost a few microseconds), at most 16 items per SM.
+    int resident = qic::decode_attention_max_active_clusters(QIC_DTYPE_BF16, head_dim, 1);
+    if (resident <= 0) resident = 3 * sm_count();
+    const double bytes = static_cast<double>(total) * tok * head_dim * 2 * 2;
+    const int max_waves = std::max(1, (16 * sm_count()) / resident);
+    const int waves = static_cast<int>(
+        std::min<double>(max_waves, std::max(1.0, std::round(bytes / (static_cast<double>(resident) * (1 << 20))))));
+    target_ctas = resident * waves;
+  }
   const long long chunk = std::max<long long>(1, (total + target_ctas - 1) / target_ctas);
   std::vector<qic::WorkItem> out;
   int part_base = 0;

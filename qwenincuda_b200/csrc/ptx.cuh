@@ -125,6 +125,17 @@ __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// One 8-byte exchange word {value, tag}: a single store and a single load, so the
+// tag and the value are seen together.
+__device__ __forceinline__ void st_word_sys(uint2* p, float v, unsigned tag) {
+  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_word_sys(const uint2* p) {
+  uint2 w;
+  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+  return w;
+}
+
 __device__ __forceinline__ unsigned ld_relaxed_gpu_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -201,7 +201,7 @@ def test_cp_rejects_bad_arguments():
     args.peer_exchange[1] = ws.ptr
     stream = torch.cuda.current_stream().cuda_stream
     assert q.lib().qic_cp_decode_attention(ctypes.byref(a), ctypes.byref(args), stream) == 4  # QIC_ERROR_WORKSPACE
-    args.exchange_bytes = 1 << 20
+    args.exchange_bytes = 1 << 30
     args.peer_exchange[0] = 0
     assert q.lib().qic_cp_decode_attention(ctypes.byref(a), ctypes.byref(args), stream) == 1
     args.peer_exchange[0] = ws.ptr
