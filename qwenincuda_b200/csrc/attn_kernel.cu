@@ -115,7 +115,9 @@ __device__ __forceinline__ uint2* cp_slot(void* base, int par, int src, int k, i
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-template <typename T, int D>
+// CP: context-parallel launch (the in-kernel exchange); a separate instantiation so
+// that single-GPU launches carry none of its code.
+template <typename T, int D, bool CP>
 __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __grid_constant__ AttnParams p) {
   using Sh = AttnShape<D>;
   constexpr int kRing = Sh::kRing;
@@ -163,10 +165,25 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (threadIdx.x == 0) record_status(p.status, QIC_DEV_BAD_PLAN);
     return;
   }
-  const int nst = st_hi - st_lo;
   const int n_stages_seq = (S + TOK - 1) / TOK;
+  // Stages of this CTA (absolute indices in the sequence): its own contiguous range
+  // [a0, a1), and, in single-sequence launches with a workspace and at least 8
+  // stages per split, a share of the first eighth of the sequence, [0, pool_n),
+  // handed out one stage at a time by the kv head's ticket counter once a warp's own
+  // stages are all issued: CTAs that start late or stream slowly take fewer of them.
+  // The own ranges split the rest evenly; the last one holds the appended token.
+  // Batched work items keep their planned range.
+  int a0 = st_lo, a1 = st_hi, pool_n = 0;
+  int* stage_ctr = nullptr;
+  if (p.plan == nullptr && p.stage_ctr != nullptr && n_stages_seq >= 8 * nsplit) {
+    pool_n = n_stages_seq / 8;
+    const int rest = n_stages_seq - pool_n;
+    a0 = pool_n + static_cast<int>(static_cast<long long>(split) * rest / nsplit);
+    a1 = pool_n + static_cast<int>(static_cast<long long>(split + 1) * rest / nsplit);
+    stage_ctr = p.stage_ctr + kvh;
+  }
   const int G = p.G;
-  const bool do_append = (p.flags & QIC_FUSE_APPEND) && st_hi == n_stages_seq;
+  const bool do_append = (p.flags & QIC_FUSE_APPEND) && a1 == n_stages_seq && a1 > a0;
   const int32_t* table = p.page_table != nullptr ? p.page_table + static_cast<size_t>(b) * p.table_bstride : nullptr;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
 
@@ -181,12 +198,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   pdl_launch_dependents();
 
   // ---- stage copies: every warp streams its own ring slots ----
-  // Stage i of this CTA lives in slot i % kRing and is consumed by warp i % 4, which
-  // also issues the slot's next stage (i + kRing) as soon as it has finished with it,
-  // so a slot never waits on another warp. Lane l < 16 copies K box l of a stage and
-  // lane 16 + l the V box l; a box is every 64-element chunk of bh token rows, at
-  // row page_table[t/P]*P + t%P when paged. The page-table entries of the warp's next
-  // stage are loaded one stage ahead.
+  // Warp w owns slots w, w+4, ... and consumes them in turn; as soon as it has
+  // finished with a slot it issues the slot's next stage itself, so a slot never
+  // waits on another warp. Lane l < 16 copies K box l of a stage and lane 16 + l the
+  // V box l; a box is every 64-element chunk of bh token rows, at row
+  // page_table[t/P]*P + t%P when paged.
+  constexpr int kSlots = kRing / kConsumerWarps;  // slots per warp
   const uint64_t pol = l2_policy_evict_first();
   if (lane == 0) {
     tma_prefetch_desc(&p.tm_k);
@@ -199,16 +216,15 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int bx = lane & 15;
   const CUtensorMap* tmap = lane < 16 ? &p.tm_k : &p.tm_v;
   const int kv_off = lane < 16 ? 0 : Sh::kKBytes;
-  const int append_stage = do_append ? nst - 1 : -1;
+  const int append_stage = do_append ? n_stages_seq - 1 : -1;
   // page-table entry holding box bx of stage j, or -1
   auto box_entry = [&](int j) -> int {
-    const int tb = (st_lo + j) * TOK + bx * bh;
-    return (j < nst && bx * bh < TOK && tb < S) ? tb / P : -1;
+    const int tb = j * TOK + bx * bh;
+    return (j >= 0 && bx * bh < TOK && tb < S) ? tb / P : -1;
   };
   auto load_entry = [&](int e) -> int { return e >= 0 ? __ldg(table + e) : 0; };
-  auto issue = [&](int j, int page) {
-    const int slot = j % kRing;
-    const int t0 = (st_lo + j) * TOK;
+  auto issue = [&](int j, int page, int slot) {
+    const int t0 = j * TOK;
     const int nbox = (min(TOK, S - t0) + bh - 1) / bh;
     const int tb = t0 + bx * bh;
     long long row = tb;
@@ -229,14 +245,34 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
                   static_cast<int>(row), kvh * Sh::kChunks, pol);
     }
   };
-  int next = warp;  // next stage this warp issues
-  int pg = table != nullptr ? load_entry(box_entry(next)) : 0;
+  // cur[k]: stage in this warp's k-th slot (issued, not yet consumed) or -1
+  int cur[kSlots], lap[kSlots];
+  int deferred = -1;  // own slot whose stage waits for the append
+  int live = 0;       // slots holding a stage
+#pragma unroll
+  for (int k = 0; k < kSlots; ++k) {
+    const int j = a0 + warp + k * kConsumerWarps;
+    cur[k] = j < a1 ? j : -1;
+    lap[k] = 0;
+    live += cur[k] >= 0 ? 1 : 0;
+  }
   // initial fill, before the inputs of the preceding kernel are waited for; the stage
-  // holding the appended token waits for the append
-  while (next < nst && next < kRing && next != append_stage) {
-    issue(next, pg);
-    next += kConsumerWarps;
-    if (table != nullptr) pg = load_entry(box_entry(next));
+  // holding the appended token waits for the append. pg_st[k]: page-table entry of
+  // the slot's next own stage (cur[k] + kRing), loaded one stage ahead.
+  int pg_st[kSlots];
+  int pg_def = 0;  // page-table entry of the deferred stage
+#pragma unroll
+  for (int k = 0; k < kSlots; ++k) {
+    pg_st[k] = 0;
+    if (cur[k] < 0) continue;
+    const int pg0 = table != nullptr ? load_entry(box_entry(cur[k])) : 0;
+    if (table != nullptr && cur[k] + kRing < a1) pg_st[k] = load_entry(box_entry(cur[k] + kRing));
+    if (cur[k] == append_stage) {
+      deferred = k;
+      pg_def = pg0;
+      continue;
+    }
+    issue(cur[k], pg0, warp + k * kConsumerWarps);
   }
 
   const int ctid = threadIdx.x;  // 0..127
@@ -292,12 +328,27 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   }
   consumer_sync();
   // the rest of the initial fill: the stage holding the appended token
-  while (next < nst && next < kRing) {
+  if (deferred >= 0) {
     fence_proxy_async_global();
-    issue(next, pg);
-    next += kConsumerWarps;
-    if (table != nullptr) pg = load_entry(box_entry(next));
+    issue(cur[deferred], pg_def, warp + deferred * kConsumerWarps);
   }
+  // Tickets of the pool: a warp asks for its next stage when it issues one, and
+  // reads the answer (and starts loading that stage's page-table entries) when it
+  // begins the following stage, so the atomic and the table load overlap compute.
+  // Tickets are taken only after griddepcontrol.wait: the counter is reset by the
+  // previous call's last merger.
+  unsigned tk_raw = 0;      // lane 0: the pending ticket
+  bool tk_pending = false;  // a ticket has been asked for and not read yet
+  int tk_next = -1;         // next pool stage of this warp (read), or -1
+  int pg_tk = 0;            // its page-table entry (lane's box)
+  // The first ticket is asked for when the warp issues its last own stage (here, if
+  // the initial copies already were); a warp with no stage of its own never reads a
+  // ticket, so it takes none.
+  auto ask_ticket = [&]() {
+    if (lane == 0) tk_raw = atomicAdd(reinterpret_cast<unsigned*>(stage_ctr), 1u);
+    tk_pending = true;
+  };
+  if (pool_n > 0 && live > 0 && a0 + warp + kSlots * kConsumerWarps >= a1) ask_ticket();
 
   // ---- B fragments of Q^T (k = dims, n = query heads of the group) ----
   const int hq = lane >> 2;       // n index held by this lane in B fragments
@@ -335,16 +386,23 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   const float sl2 = p.scale_log2;
   bool ok = true;
-  int i = warp;
 
 #pragma unroll 1
-  for (; i < nst; i += kConsumerWarps) {
-    const int slot = i % kRing;
-    if (!__all_sync(kFullMask, mbar_wait(&full[slot], (i / kRing) & 1, deadline))) {
+  for (int k = 0; live > 0; k = (k + 1 == kSlots) ? 0 : k + 1) {
+    if (cur[k] < 0) continue;
+    const int i = cur[k];
+    const int slot = warp + k * kConsumerWarps;
+    if (!__all_sync(kFullMask, mbar_wait(&full[slot], lap[k] & 1, deadline))) {
       ok = false;
       break;
     }
-    const int t0 = (st_lo + i) * TOK;
+    if (tk_pending) {
+      const int v = static_cast<int>(__shfl_sync(kFullMask, tk_raw, 0));
+      tk_next = v < pool_n ? v : -1;
+      if (tk_next >= 0 && table != nullptr) pg_tk = load_entry(box_entry(tk_next));
+      tk_pending = false;
+    }
+    const int t0 = i * TOK;
     const int nvalid = min(TOK, S - t0);
     uint8_t* sk = ring + slot * Sh::kStageBytes;
     const uint32_t bk = smem_u32(sk);
@@ -444,11 +502,24 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
     __syncwarp();
-    // refill this slot with the warp's next stage (i + kRing) right away
-    if (next < nst) {
-      issue(next, pg);
-      next += kConsumerWarps;
-      if (table != nullptr) pg = load_entry(box_entry(next));
+    ++lap[k];
+    // refill this slot right away: the slot's next own stage, else the warp's next
+    // pool stage, if any
+    if (i >= a0 && i + kRing < a1) {  // (a pool stage has no own continuation)
+      const int j = i + kRing;
+      issue(j, pg_st[k], slot);
+      cur[k] = j;
+      if (table != nullptr && j + kRing < a1) pg_st[k] = load_entry(box_entry(j + kRing));
+      // the warp's last own stage is issued: ask for a pool stage for the next refill
+      if (pool_n > 0 && j + kConsumerWarps >= a1) ask_ticket();
+    } else if (tk_next >= 0) {
+      issue(tk_next, pg_tk, slot);
+      cur[k] = tk_next;
+      tk_next = -1;
+      ask_ticket();
+    } else {
+      cur[k] = -1;
+      --live;
     }
   }
   if (!ok) {
@@ -458,8 +529,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     // wait (bounded) for this warp's copies still in flight before the CTA exits
     const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
-#pragma unroll 1
-    for (int j = i; j < next; j += kConsumerWarps) mbar_wait(&full[j % kRing], (j / kRing) & 1, dl2);
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k)
+      if (cur[k] >= 0) mbar_wait(&full[warp + k * kConsumerWarps], lap[k] & 1, dl2);
     __syncwarp();
   }
   // full row sums per head column
@@ -525,7 +597,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const size_t qoff = static_cast<size_t>(kvh) * G * D;  // first output row of this group
   const int GD = G * D;
   const int pf = partial_floats(G, D);
-  const bool cp = p.cp_world > 0;
+  constexpr bool cp = CP;
   unsigned cp_e = 0;  // exchange epoch of this call (slice mergers, context parallel)
   // Destination of the final value o of output idx (head h, log-sum-exp lse): the
   // output or the caller's fp32 partial (QIC_PARTIAL_OUT).
@@ -552,7 +624,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
   }
-  if (nsplit == 1) return;
+  if (nsplit == 1) {
+    // every warp of the kv head's only CTA is past its stage loop: ready for the next call
+    if (stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
+    return;
+  }
 
   // ---- merge the partials of this cluster through distributed shared memory ----
   cluster_sync_all();  // every CTA of the cluster has its partial in shared memory
@@ -560,6 +636,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int rank = split % C;
   const int cid = split / C;
   const int nclust = nsplit / C;
+  // a kv head that is one cluster is past every stage loop: reset its ticket counter
+  if (nclust == 1 && rank == 0 && stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
@@ -653,7 +731,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         emit(idx, h, sum > 0.0f ? o / sum : 0.0f, sum > 0.0f ? mx + log2f(sum) : -INFINITY,
              idx == lo || idx - h * D == 0);
       }
-      if (ctid == 0) p.counters[counter] = 0;  // ready for the next call
+      if (ctid == 0) {
+        p.counters[counter] = 0;  // ready for the next call
+        // every cluster of this kv head has arrived: past every stage loop
+        if (rank == 0 && stage_ctr != nullptr) *stage_ctr = 0;
+      }
     }
   }
   if (cp && cid == 0) {
@@ -757,6 +839,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (late) record_status(p.status, QIC_DEV_PEER_TIMEOUT);
     // the last slice merger of this call advances the epoch for the next call
     consumer_sync();
+    // every cluster of this rank's kv head has contributed: past every stage loop
+    if (nclust > 1 && rank == 0 && stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
     if (ctid == 0) {
       const unsigned prev = atomicAdd(p.cp_done, 1u);
       if (prev == static_cast<unsigned>(p.cp_mergers) - 1u) {
@@ -830,19 +914,29 @@ size_t decode_attention_smem_bytes(int head_dim) {
 }
 
 template <typename T, int D>
-static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t stream) {
+static cudaError_t configure_typed() {
   static unsigned long long configured = 0;  // one bit per device ordinal
   const int smem = AttnShape<D>::kSmemBytes;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 64 && !(configured & (1ull << dev))) {
-    e = cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    configured |= 1ull << dev;
-  }
+  if (dev < 64 && (configured & (1ull << dev))) return cudaSuccess;
+  e = cudaFuncSetAttribute(decode_attn_kernel<T, D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<T, D, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<T, D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<T, D, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && dev < 64) configured |= 1ull << dev;
+  return e;
+}
+
+template <typename T, int D>
+static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t stream) {
+  const int smem = AttnShape<D>::kSmemBytes;
+  cudaError_t e = configure_typed<T, D>();
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
@@ -857,7 +951,8 @@ static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t str
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, D>, p);
+  e = p.cp_world > 0 ? cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, D, true>, p)
+                     : cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, D, false>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -870,9 +965,7 @@ static int max_active_clusters_typed(int cluster) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || cluster < 1 || cluster > kMaxCluster) return 0;
   if (cache[dev][cluster] != 0) return cache[dev][cluster];
   const int smem = AttnShape<D>::kSmemBytes;
-  if (cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_attn_kernel<T, D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-    return 0;
+  if (configure_typed<T, D>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster, 1, 1);
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
@@ -885,7 +978,7 @@ static int max_active_clusters_typed(int cluster) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<T, D>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<T, D, false>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }

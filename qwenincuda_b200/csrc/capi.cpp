@@ -353,7 +353,8 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   if (n_clusters > 1) {
     const size_t need = qic::kWsPartialOffset +
                         static_cast<size_t>(Hkv) * n_clusters * qic::partial_floats(G, D) * sizeof(float);
-    if (a->workspace_bytes < need || Hkv * cluster > qic::kMaxCounters) return QIC_ERROR_WORKSPACE;
+    if (a->workspace_bytes < need || Hkv * cluster > qic::kMaxCounters - qic::kMaxStageCounters)
+      return QIC_ERROR_WORKSPACE;
   }
   if (a->workspace != nullptr) {
     char* ws = static_cast<char*>(a->workspace);
@@ -361,7 +362,9 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     if (a->workspace_bytes >= qic::kWsPartialOffset) {
       p.counters = reinterpret_cast<int*>(ws + qic::kWsHeader);
       p.part = reinterpret_cast<float*>(ws + qic::kWsPartialOffset);
-      p.num_counters = std::min(Hkv * cluster, qic::kMaxCounters);
+      p.num_counters = std::min(Hkv * cluster, qic::kMaxCounters - qic::kMaxStageCounters);
+      if (Hkv <= qic::kMaxStageCounters)
+        p.stage_ctr = p.counters + (qic::kMaxCounters - qic::kMaxStageCounters);
       p.part_slots = static_cast<int>(std::min<size_t>(
           INT32_MAX, (a->workspace_bytes - qic::kWsPartialOffset) / (qic::partial_floats(G, D) * sizeof(float))));
     }

@@ -23,6 +23,9 @@ constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s bound on every dev
 constexpr size_t kWsHeader = 256;
 constexpr int kMaxCounters = 8192;
 constexpr size_t kWsPartialOffset = kWsHeader + static_cast<size_t>(kMaxCounters) * sizeof(int);
+// The last kMaxStageCounters counters of that region are the stage-pool ticket
+// counters of single-sequence launches (one per kv head), never merge counters.
+constexpr int kMaxStageCounters = 64;
 
 // Tokens per TMA pipeline stage: one stage is 16 KB of K+V for head_dim 128/256
 // (32 / 16 tokens) and 8 KB for head_dim 64 (32 tokens).
@@ -93,6 +96,7 @@ struct AttnParams {
   uint64_t timeout_ns;
   long long rope_pos;                // RoPE position of q and the appended k (single-sequence launches)
   float* part_out;                   // QIC_PARTIAL_OUT: [Hkv][partial_floats] instead of out
+  int* stage_ctr;                    // per kv head ticket counters of the stage pool, or null
   // context parallelism (cp_world == 0: off)
   int cp_rank, cp_world;
   int cp_mergers;                    // slice mergers per call on this rank: Hkv * kCpSlices

@@ -245,3 +245,28 @@ def test_fused_decode_step_matches_reference_chain(name, paged):
     assert torch.equal(mine.v_cache.view(torch.int16), theirs.v_cache.view(torch.int16))
     ok, err, idx = allclose_report(out, want, ATOL, RTOL)
     assert ok, f"max abs err {err} at {idx}"
+
+
+def test_stage_pool_counters_reset_between_calls():
+    """Long sequences take part of their stages from a per-kv-head ticket counter in
+    the workspace; the last merger resets it. Calls of two shapes alternating on one
+    workspace (several clusters per kv head, and one CTA per kv head) stay correct."""
+    w = q.Workspace(32, 8, 128, 16385)
+    shapes = [(32, 8, 128, 16385, 16, 0), (16, 4, 128, 5000, 16, 1), (32, 8, 128, 9001, 32, 16)]
+    inputs = {}
+    for H, Hkv, d, S, P, splits in shapes:
+        qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=S)
+        inputs[S] = (qv, kc, vc, table, _ref(qv, kc, vc, H, Hkv, d, S, table, P))
+    for rep in range(3):
+        for H, Hkv, d, S, P, splits in shapes:
+            qv, kc, vc, table, want = inputs[S]
+            out = torch.full((H * d,), float("nan"), device="cuda", dtype=torch.bfloat16)
+            q.decode_attention(q=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d,
+                               seq_len=S, page_table=table, page_size=P, workspace=w, num_splits=splits)
+            torch.cuda.synchronize()
+            assert w.status() == 0
+            ok, err, idx = allclose_report(out, want, ATOL, RTOL)
+            assert ok, f"call {rep} S={S}: max abs err {err} at {idx}"
+    # the ticket counters (the last 64 counters) are back at zero
+    top = w.buf[256 + (8192 - 64) * 4: 256 + 8192 * 4].view(torch.int32)
+    assert int(top.abs().sum()) == 0
