@@ -20,8 +20,9 @@ batch partitioned by K/V bytes (strong scaling: total bytes / the slowest rank's
 time). --workload qwen3_8b_s131073 or qwen3_8b_batch64 with N > 1 makes those the
 line's value.
 
-Other workloads (--workload): qwen3_0p6b_s1025, qwen35_gated_s32769 (d=256 with the
-output gate), qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step;
+Other workloads (--workload): qwen3_0p6b_s1025 (one layer), qwen35_gated_s32769 (d=256
+with the output gate; 8 layers chained like the full-attention layers of a hybrid
+stack, each with its own 32K cache), qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step;
 state bytes), qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64
 (64 sequences, lengths 512..32768, one shared page pool, one batched launch).
 
@@ -285,7 +286,7 @@ def gdn_workload():
 
 def pair_workload():
     gdn = gdn_workload()
-    att = attention_workload("qwen35_gated_s32769", "paged")
+    att = attention_workload("qwen35_gated_s32769", "paged", layers=1)
 
     def step():
         gdn["step"]()

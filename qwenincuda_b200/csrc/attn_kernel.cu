@@ -707,19 +707,19 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
 #pragma unroll 1
       for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
         const int h = idx / D;
-        // online log-sum-exp over the cluster partials, four loads in flight at a time
+        // online log-sum-exp over the cluster partials, eight loads in flight at a time
         float mx = -INFINITY, sum = 0.0f, o = 0.0f;
 #pragma unroll 1
-        for (int k0 = 0; k0 < nclust; k0 += 4) {
-          float lk[4], ok[4];
+        for (int k0 = 0; k0 < nclust; k0 += 8) {
+          float lk[8], ok[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 8; ++u) {
             const int k = k0 + u;
             lk[u] = k < nclust ? __ldcg(g0 + static_cast<size_t>(k) * pf + GD + h) : -INFINITY;
             ok[u] = k < nclust ? __ldcg(g0 + static_cast<size_t>(k) * pf + idx) : 0.0f;
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 8; ++u) {
             const float mn = fmaxf(mx, lk[u]);
             if (mn == -INFINITY) continue;
             const float sc = exp2f(mx - mn), w = exp2f(lk[u] - mn);

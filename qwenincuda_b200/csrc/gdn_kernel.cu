@@ -64,6 +64,25 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   const T* conv_w = static_cast<const T*>(a.conv_w);
   float* conv_state = a.conv_state;
 
+  // ---- 0. every global load that does not depend on another is issued first, so
+  // the state block, the gate scalars and the output-gate inputs arrive together
+  // with the conv inputs instead of in sequence ----
+  const int quad = tid % QUADS;
+  const int rg = tid / QUADS;
+  float* state = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv + cb * NC + quad * 4;
+  float4 s[RPT];
+#pragma unroll
+  for (int r = 0; r < RPT; ++r) s[r] = *reinterpret_cast<const float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv);
+  const T bv_raw = static_cast<const T*>(a.b)[vh];
+  const T av_raw = static_cast<const T*>(a.a)[vh];
+  const T dt_raw = static_cast<const T*>(a.dt_bias)[vh];
+  const T al_raw = static_cast<const T*>(a.a_log)[vh];
+  T z_raw = T(), nw_raw = T();
+  if (tid < NC) {
+    z_raw = static_cast<const T*>(a.z)[static_cast<size_t>(vh) * kGdnDv + cb * NC + tid];
+    nw_raw = static_cast<const T*>(a.norm_w)[cb * NC + tid];
+  }
+
   // ---- 1. causal conv + SiLU from the old conv state ----
   // thread t: q channel t and k channel t of key head kh; v channel t (t < NC)
   float win_q[8], win_k[8], win_v[8];
@@ -87,28 +106,9 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   k_s[tid] = conv_channel(ck, win_k);
   if (tid < NC) v_s[tid] = conv_channel(cv, win_v);
 
-  // every CTA of the cluster has read the old conv state past this point
-  cluster.sync();
-
-  // ---- 2. new conv state: q/k channels by the first value head's CTAs, v by owner ----
-  if (vloc == 0) {
-    constexpr int QK_PER = kGdnDk / CB;
-    if (tid >= cb * QK_PER && tid < (cb + 1) * QK_PER) {
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        if (t < K) {
-          conv_state[static_cast<size_t>(cq) * K + t] = win_q[t];
-          conv_state[static_cast<size_t>(ck) * K + t] = win_k[t];
-        }
-      }
-    }
-  }
-  if (tid < NC) {
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (t < K) conv_state[static_cast<size_t>(cv) * K + t] = win_v[t];
-    }
-  }
+  // every CTA of the cluster has read the old conv state past this point (first
+  // phase of the cluster barrier; the conv-state writes wait for it further down)
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   __syncthreads();
 
   // ---- 3. L2 norms of q and k, q scale (src/model.cpp:721-735) ----
@@ -138,19 +138,13 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   __syncthreads();
 
   // ---- 4. gates (src/model.cpp:739-742) ----
-  const float bval = to_f32<T>(static_cast<const T*>(a.b)[vh]);
+  const float bval = to_f32<T>(bv_raw);
   const float beta = 1.0f / (1.0f + expf(-bval));
-  const float av = to_f32<T>(static_cast<const T*>(a.a)[vh]) + to_f32<T>(static_cast<const T*>(a.dt_bias)[vh]);
+  const float av = to_f32<T>(av_raw) + to_f32<T>(dt_raw);
   const float softp = log1pf(expf(av));
-  const float g = expf(-expf(to_f32<T>(static_cast<const T*>(a.a_log)[vh])) * softp);
+  const float g = expf(-expf(to_f32<T>(al_raw)) * softp);
 
-  // ---- 5. state block: rows i = rg + RG*r, columns cb*NC + 4*quad .. +3 ----
-  const int quad = tid % QUADS;
-  const int rg = tid / QUADS;
-  float* state = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv + cb * NC + quad * 4;
-  float4 s[RPT];
-#pragma unroll
-  for (int r = 0; r < RPT; ++r) s[r] = *reinterpret_cast<const float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv);
+  // ---- 5. state block (loaded at the start): rows i = rg + RG*r, columns cb*NC + 4*quad .. +3 ----
 
   auto block_colsum = [&](float4 part) {
     // sum `part` over all threads with the same quad, result in col_s[4*quad + 0..3]
@@ -225,7 +219,28 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (tid == 0) ssq_part = ss;
   }
-  cluster.sync();
+  // every CTA has read the old conv state: write the new one (q/k channels by the
+  // first value head's CTAs, v channels by their owner)
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+  if (vloc == 0) {
+    constexpr int QK_PER = kGdnDk / CB;
+    if (tid >= cb * QK_PER && tid < (cb + 1) * QK_PER) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        if (t < K) {
+          conv_state[static_cast<size_t>(cq) * K + t] = win_q[t];
+          conv_state[static_cast<size_t>(ck) * K + t] = win_k[t];
+        }
+      }
+    }
+  }
+  if (tid < NC) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t < K) conv_state[static_cast<size_t>(cv) * K + t] = win_v[t];
+    }
+  }
+  cluster.sync();  // every CTA's ssq_part is written
   float ss = 0.0f;
 #pragma unroll
   for (int c = 0; c < CB; ++c) {
@@ -236,9 +251,9 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   if (tid < NC) {
     const int j = cb * NC + tid;
     const float normed = __fmul_rn(col_s[tid], inv);
-    const float zv = to_f32<T>(static_cast<const T*>(a.z)[static_cast<size_t>(vh) * kGdnDv + j]);
+    const float zv = to_f32<T>(z_raw);
     const float gate = zv / (1.0f + expf(-zv));
-    const float ww = to_f32<T>(static_cast<const T*>(a.norm_w)[j]);
+    const float ww = to_f32<T>(nw_raw);
     static_cast<T*>(a.out)[static_cast<size_t>(vh) * kGdnDv + j] = from_f32<T>(__fmul_rn(__fmul_rn(normed, ww), gate));
   }
   // keep this CTA's shared memory alive until every peer has read ssq_part

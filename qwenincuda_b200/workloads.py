@@ -14,7 +14,10 @@ distributions of the configurations below.
                      state ~ N(0, 0.02^2), a,b ~ N(0,1), A_log = log U[1,16],
                      dt_bias ~ N(0, 0.1^2)
   qwen35_gated_s32769  16 q heads, 4 kv heads, d=256, 32768 cached + append at
-                     32768 (S=32769), q_gate ~ N(0,1)
+                     32768 (S=32769), q_gate ~ N(0,1); 8 layers, each with its own
+                     cache: the gated-attention layers of a 32-layer hybrid stack
+                     with one full-attention layer in four (the reference takes the
+                     layer kinds from the model config, src/model.cpp:368-389)
   qwen3_8b_s131073   32/8 heads, d=128, 131072 cached + append (S=131073), page 16,
                      shuffled table
 """
@@ -63,7 +66,7 @@ class AttnConfig:
 CONFIGS = {
     "qwen3_0p6b_s1025": AttnConfig("qwen3_0p6b_s1025", 16, 8, 128, 1025, kv_std=0.5, seed=1),
     "qwen3_8b_s8192": AttnConfig("qwen3_8b_s8192", 32, 8, 128, 8192, layers=36, seed=2),
-    "qwen35_gated_s32769": AttnConfig("qwen35_gated_s32769", 16, 4, 256, 32769, gate=True, seed=3),
+    "qwen35_gated_s32769": AttnConfig("qwen35_gated_s32769", 16, 4, 256, 32769, layers=8, gate=True, seed=3),
     "qwen3_8b_s131073": AttnConfig("qwen3_8b_s131073", 32, 8, 128, 131073, seed=4),
 }
 
