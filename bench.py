@@ -217,6 +217,10 @@ def attention_workload(name, layout, layers=None):
     cfg = CONFIGS[name]
     inp = make_attention_inputs(cfg, paged=(layout == "paged"), layers=layers)
     L_ = inp.q.shape[0]
+    # the step's per-layer inputs (q, k_new, v_new of every layer) live in one device
+    # buffer, so the end-to-end step moves them with one host-to-device copy
+    packed, views = _pack([inp.q, inp.k_new, inp.v_new])
+    inp.q, inp.k_new, inp.v_new = views
     ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
     fns = []
     for layer in range(L_):
@@ -233,25 +237,35 @@ def attention_workload(name, layout, layers=None):
         for f in fns:
             f()
 
-    hq = inp.q.cpu().pin_memory()
-    hk = inp.k_new.cpu().pin_memory()
-    hv = inp.v_new.cpu().pin_memory()
+    hin = packed.cpu().pin_memory()
     ho = torch.empty_like(inp.out, device="cpu").pin_memory()
 
     def e2e():
-        inp.q.copy_(hq, non_blocking=True)
-        inp.k_new.copy_(hk, non_blocking=True)
-        inp.v_new.copy_(hv, non_blocking=True)
+        packed.copy_(hin, non_blocking=True)
         step()
         ho.copy_(inp.out, non_blocking=True)
 
     per_layer = cfg.kv_read_bytes() + cfg.append_bytes()
     return dict(step=step, bytes=per_layer * L_, launches=L_, bytes_per_launch=per_layer,
-                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2), kernel="decode_attn_kernel",
-                status=ws.status, keep=(inp, ws),
+                e2e=(e2e, hin.numel() * hin.element_size(), ho.numel() * ho.element_size()),
+                kernel="decode_attn_kernel", status=ws.status, keep=(inp, ws, packed),
                 config={"layout": layout, "page_size": cfg.page_size, "layers": L_, "seq_len": cfg.seq_len,
                         "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
                         "gate": cfg.gate})
+
+
+def _pack(tensors):
+    """One device buffer holding `tensors` (same dtype) back to back, and views of it
+    with their shapes (filled with their values)."""
+    total = sum(t.numel() for t in tensors)
+    buf = torch.empty(total, device=tensors[0].device, dtype=tensors[0].dtype)
+    views, at = [], 0
+    for t in tensors:
+        v = buf[at:at + t.numel()].view(t.shape)
+        v.copy_(t)
+        views.append(v)
+        at += t.numel()
+    return buf, views
 
 
 def gdn_workload():
@@ -260,6 +274,8 @@ def gdn_workload():
 
     cfg = GdnConfig()
     t = make_gdn_inputs(cfg)
+    packed, views = _pack([t["qkv"], t["z"], t["b"], t["a"]])  # one host-to-device copy per step
+    t["qkv"], t["z"], t["b"], t["a"] = views
     g = q.GdnArgs()
     g.dtype = 1
     g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
@@ -267,18 +283,17 @@ def gdn_workload():
     for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state", "out"):
         setattr(g, k, t[k].data_ptr())
     step = _call(q.lib().qic_gated_delta_decode, g)
-    hin = {k: t[k].cpu().pin_memory() for k in ("qkv", "z", "b", "a")}
+    hin = packed.cpu().pin_memory()
     hout = torch.empty_like(t["out"], device="cpu").pin_memory()
 
     def e2e():
-        for k, v in hin.items():
-            t[k].copy_(v, non_blocking=True)
+        packed.copy_(hin, non_blocking=True)
         step()
         hout.copy_(t["out"], non_blocking=True)
 
-    h2d = sum(v.numel() * 2 for v in hin.values())
+    h2d = hin.numel() * hin.element_size()
     return dict(step=step, bytes=cfg.state_bytes(), launches=1, bytes_per_launch=cfg.state_bytes(),
-                e2e=(e2e, h2d, hout.numel() * 2), kernel="gated_delta_kernel", status=lambda: 0, keep=(t, g),
+                e2e=(e2e, h2d, hout.numel() * 2), kernel="gated_delta_kernel", status=lambda: 0, keep=(t, g, packed),
                 config={"num_k_heads": cfg.num_k_heads, "num_v_heads": cfg.num_v_heads, "k_head_dim": 128,
                         "v_head_dim": 128, "conv_dim": cfg.conv_dim, "conv_kernel": cfg.conv_kernel,
                         "state": "fp32, resident on the device"})
@@ -318,6 +333,7 @@ def batched_workload(world, rank):
     lens = [all_lens[i] for i in mine]
     cfg = dataclasses.replace(cfg, pool_tokens=(cfg.pool_tokens + world - 1) // world, seed=cfg.seed + 101 * rank)
     inp = make_batched_inputs(cfg, seq_lens=lens)
+    packed, (inp["q"], inp["k_new"], inp["v_new"]) = _pack([inp["q"], inp["k_new"], inp["v_new"]])
     plan = q.BatchPlan(lens, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
     a = q.ops.batch_decode_args(plan=plan, q=inp["q"], k_cache=inp["k_cache"], v_cache=inp["v_cache"],
                                 block_tables=inp["block_tables"], out=inp["out"], num_heads=cfg.num_heads,
@@ -325,22 +341,18 @@ def batched_workload(world, rank):
                                 q_norm_w=inp["q_norm_w"], k_norm_w=inp["k_norm_w"], k_new=inp["k_new"],
                                 v_new=inp["v_new"], fuse_q=True, fuse_append=True, cache_tokens=inp["cache_tokens"])
     step = _call(q.lib().qic_batch_decode_attention, a)
-    hq = inp["q"].cpu().pin_memory()
-    hk = inp["k_new"].cpu().pin_memory()
-    hv = inp["v_new"].cpu().pin_memory()
+    hin = packed.cpu().pin_memory()
     ho = torch.empty_like(inp["out"], device="cpu").pin_memory()
 
     def e2e():
-        inp["q"].copy_(hq, non_blocking=True)
-        inp["k_new"].copy_(hk, non_blocking=True)
-        inp["v_new"].copy_(hv, non_blocking=True)
+        packed.copy_(hin, non_blocking=True)
         step()
         ho.copy_(inp["out"], non_blocking=True)
 
     nbytes = batched_bytes(lens, cfg.kv_dim)
     return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes, partitioned=world > 1,
-                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2), kernel="decode_attn_kernel",
-                status=plan.status, keep=(inp, plan, a),
+                e2e=(e2e, hin.numel() * 2, ho.numel() * 2), kernel="decode_attn_kernel",
+                status=plan.status, keep=(inp, plan, a, packed),
                 config={"batch": cfg.batch, "seq_lens": f"U[{cfg.min_len},{cfg.max_len}]+1, seed {BatchConfig().seed}",
                         "sequences_on_rank0": len(lens) if rank == 0 else None, "ranks": world,
                         "tokens_total": sum(all_lens), "page_size": cfg.page_size, "pool_tokens_per_rank": inp["cache_tokens"],
@@ -374,6 +386,7 @@ def cp_workload(world, rank, with_allgather=True):
     qv = torch.randn(H * d, generator=gs, device="cuda").to(dtype)
     kn = torch.randn(Hkv * d, generator=gs, device="cuda").to(dtype)
     vn = (torch.randn(Hkv * d, generator=gs, device="cuda") * cfg.kv_std).to(dtype)
+    packed, (qv, kn, vn) = _pack([qv, kn, vn])  # one host-to-device copy per step
     ones = torch.ones(d, device="cuda", dtype=dtype)
     out = torch.zeros(H * d, device="cuda", dtype=dtype)
     ws = q.Workspace(H, Hkv, d, n)
@@ -391,13 +404,11 @@ def cp_workload(world, rank, with_allgather=True):
         if rc != 0:
             raise q.QicError(rc, "qic_cp_decode_attention")
 
-    hq, hk, hv = qv.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    hin = packed.cpu().pin_memory()
     ho = torch.empty_like(out, device="cpu").pin_memory()
 
     def e2e():
-        qv.copy_(hq, non_blocking=True)
-        kn.copy_(hk, non_blocking=True)
-        vn.copy_(hv, non_blocking=True)
+        packed.copy_(hin, non_blocking=True)
         step()
         ho.copy_(out, non_blocking=True)
 
@@ -423,9 +434,9 @@ def cp_workload(world, rank, with_allgather=True):
 
         allgather = ag_step
     return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes, partitioned=True,
-                e2e=(e2e, (hq.numel() + hk.numel() + hv.numel()) * 2, ho.numel() * 2),
+                e2e=(e2e, hin.numel() * 2, ho.numel() * 2),
                 kernel="decode_attn_kernel (fused NVLink exchange)", status=ws.status, allgather=allgather,
-                keep=(kc, vc, table, qv, kn, vn, out, ws, group, a),
+                keep=(kc, vc, table, qv, kn, vn, out, ws, group, a, packed),
                 config={"seq_len": S, "page_size": P, "num_heads": H, "num_kv_heads": Hkv, "head_dim": d,
                         "ranks": world, "shard_tokens_rank0": cpm.shard_tokens(S, P, world)[0][1],
                         "exchange": "in-kernel NVLink stores + system-scope flags, log-sum-exp merge"})

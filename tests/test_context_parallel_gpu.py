@@ -6,8 +6,8 @@
   within max-abs 2e-3 / rel 1e-2, and the appended rows are byte-identical.
 * The fused exchange with one rank equals the plain call bit for bit, call after call
   (epoch and parity bookkeeping).
-* Failure detection: a peer that never publishes (its flag is never set) makes the
-  bounded wait give up; the kernel records QIC_DEV_PEER_TIMEOUT, leaves the output
+* Failure detection: a peer that never publishes (no exchange word ever carries the
+  call's tag) makes the bounded wait give up; the kernel records QIC_DEV_PEER_TIMEOUT, leaves the output
   untouched and the context stays usable.
 """
 import ctypes
@@ -149,8 +149,8 @@ def test_fused_exchange_world1_equals_plain_call():
 
 
 def test_peer_that_never_publishes_times_out():
-    """World 2 on one GPU with only rank 0 running: the flags of rank 1 in rank 0's
-    exchange buffer are never set, so the bounded wait (50 ms) gives up."""
+    """World 2 on one GPU with only rank 0 running: rank 1's words in rank 0's exchange
+    buffer never carry the call's tag, so the bounded wait (50 ms) gives up."""
     S = 2048
     k, v, qv, kn, vn, w = _sequence(S, seed=33)
     kc, tab = _paged(k, seed=6)
