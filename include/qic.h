@@ -210,14 +210,14 @@ typedef struct qic_cp_args {
 /* Bytes of one rank's exchange buffer. */
 size_t qic_cp_exchange_bytes(int num_heads, int num_kv_heads, int head_dim, int world);
 
-/* Decode attention of one shard of a sequence, fused with the exchange: every
- * 8-CTA cluster stores its merged (o, lse) slices into every rank's exchange buffer
- * over NVLink as 8-byte words {value, call tag} (one store each: no fence or flag),
- * and one CTA per (kv head, slice) on each rank polls the words of every (rank,
- * cluster) contribution (bounded wait), merges them by log-sum-exp and writes out
- * (with the gate). At most 16 clusters per kv head on a rank. Every rank calls it
- * once per step with the same shapes, cluster size (8) and number of calls;
- * args->workspace is required (it keeps the call epoch).
+/* Decode attention of one shard of a sequence, fused with the exchange: the rank's
+ * (o, lse) partial of every (kv head, slice), merged over the rank's 8-CTA
+ * clusters, is stored into every rank's exchange buffer over NVLink as 8-byte words
+ * {value, call tag} (one store each: no fence or flag); the CTA that produced the
+ * slice polls the words of every rank's contribution (bounded wait), merges them by
+ * log-sum-exp and writes out (with the gate). Every rank calls it once per step
+ * with the same shapes, cluster size (8) and number of calls; args->workspace is
+ * required (it keeps the call epoch).
  * Shard layout: each rank's args describe its own tokens (seq_len, page_table or
  * contiguous rows); q is the same on every rank; QIC_EXPLICIT_POSITION gives the
  * global position for RoPE; the rank holding the last token sets QIC_FUSE_APPEND.

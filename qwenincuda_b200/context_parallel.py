@@ -3,12 +3,11 @@
 Long single sequences (context parallelism): the sequence's pages are cut into
 contiguous ranges, one per rank (shard_tokens). Every rank keeps the K/V pages and
 block table of its own range and calls qic_cp_decode_attention with the same q;
-inside the kernel every thread-block cluster stores its merged (o, lse) slice into
-every rank's exchange buffer over NVLink as tagged 8-byte words, and one CTA per
-(kv head, slice) on each rank polls the words of all (rank, cluster) contributions
-(bounded wait) and merges them by log-sum-exp, so every rank ends with the full
-output. The rank that
-holds the last token performs the append. ExchangeGroup allocates this rank's
+inside the kernel the rank's (o, lse) partial of each (kv head, slice), merged over
+the rank's clusters, is stored into every rank's exchange buffer over NVLink as
+tagged 8-byte words, and the CTA that produced that slice polls the words of every
+rank's contribution (bounded wait) and merges them by log-sum-exp, so every rank
+ends with the full output. The rank that holds the last token performs the append. ExchangeGroup allocates this rank's
 exchange buffer and maps every other rank's buffer into this process with CUDA IPC;
 the IPC handles travel over torch.distributed (any backend, gloo included).
 
@@ -144,11 +143,11 @@ class ExchangeGroup:
 
 def exchange_bytes_host(num_heads: int, num_kv_heads: int, head_dim: int, world: int) -> int:
     """Size of one rank's exchange buffer, computed on the host (the layout of
-    qic_cp_exchange_bytes): [2 parities][world][16 clusters][Hkv][8 slices] contributions
-    of ceil(G*d/8) + 2 eight-byte words (outputs, then two log-sum-exp words)."""
+    qic_cp_exchange_bytes): [2 parities][world][Hkv][8 slices] contributions of
+    ceil(G*d/8) + 2 eight-byte words (outputs, then two log-sum-exp words)."""
     g = num_heads // num_kv_heads
     words = (g * head_dim + 7) // 8 + 2
-    return 2 * world * 16 * num_kv_heads * 8 * words * 8
+    return 2 * world * num_kv_heads * 8 * words * 8
 
 
 def cp_decode_attention(group: ExchangeGroup, stream=None, **kw) -> None:

@@ -104,11 +104,11 @@ __device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, float o)
   ob[i] = ot;
 }
 
-// Contribution (parity, source rank, cluster k, kv head, slice c) in the exchange
-// buffer at `base`: cp_slice_words 8-byte words.
-__device__ __forceinline__ uint2* cp_slot(void* base, int par, int src, int k, int world, int Hkv, int kvh, int c,
+// Contribution (parity, source rank, kv head, slice c) in the exchange buffer at
+// `base`: cp_slice_words 8-byte words.
+__device__ __forceinline__ uint2* cp_slot(void* base, int par, int src, int world, int Hkv, int kvh, int c,
                                           int words) {
-  const size_t i = ((((static_cast<size_t>(par) * world + src) * kCpMaxClusters + k) * Hkv + kvh) * kCpSlices + c);
+  const size_t i = ((static_cast<size_t>(par) * world + src) * Hkv + kvh) * kCpSlices + c;
   return static_cast<uint2*>(base) + i * words;
 }
 
@@ -641,13 +641,22 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
-  // context parallel: this cluster's slice goes to every rank as one contribution
+  // context parallel: this rank's merged slice (after the cross-cluster merge when the
+  // kv head spans several clusters) goes to every rank as one contribution
   const int cpw = cp_slice_words(G, D);
   unsigned cp_tag = 0;
   if (cp) {
     cp_e = ld_relaxed_gpu_u32(p.cp_epoch) + 1;
-    cp_tag = ((cp_e & 0xffffffu) << 8) | static_cast<unsigned>(nclust);
+    cp_tag = ((cp_e & 0xffffffu) << 8) | 1u;
   }
+  auto cp_push = [&](int idx, float o, float lse) {
+    for (int r = 0; r < p.cp_world; ++r) {
+      uint2* slot = cp_slot(p.cp_peer[r], cp_e & 1, p.cp_rank, p.cp_world, p.Hkv, kvh, rank, cpw);
+      st_word_sys(slot + (idx - lo), o, cp_tag);
+      if (idx == lo) st_word_sys(slot + cpw - 2, lse, cp_tag);
+      if (idx == hi - 1) st_word_sys(slot + cpw - 1, lse, cp_tag);
+    }
+  };
   float* gslot = p.part + static_cast<size_t>(part_base + cid) * pf;  // [o: G*D][lse: G]
 #pragma unroll 1
   for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
@@ -676,14 +685,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
     o = sum > 0.0f ? o / sum : 0.0f;
-    if (cp) {
-      const float lse = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
-      for (int r = 0; r < p.cp_world; ++r) {
-        uint2* slot = cp_slot(p.cp_peer[r], cp_e & 1, p.cp_rank, cid, p.cp_world, p.Hkv, kvh, rank, cpw);
-        st_word_sys(slot + (idx - lo), o, cp_tag);
-        if (idx == lo) st_word_sys(slot + cpw - 2, lse, cp_tag);
-        if (idx == hi - 1) st_word_sys(slot + cpw - 1, lse, cp_tag);
-      }
+    if (cp && nclust == 1) {
+      cp_push(idx, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY);
     } else if (nclust == 1) {
       emit(idx, h, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY, idx == lo || idx - h * D == 0);
     } else {
@@ -693,7 +696,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   }
   // every CTA of the cluster has read the partials it needs from this one
   cluster_sync_all();
-  if (nclust > 1 && !cp) {
+  if (nclust > 1) {
     // ---- merge the cluster partials of this slice: last arriving cluster ----
     consumer_sync();
     const int counter = (b * p.Hkv + kvh) * C + rank;
@@ -728,8 +731,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
             mx = mn;
           }
         }
-        emit(idx, h, sum > 0.0f ? o / sum : 0.0f, sum > 0.0f ? mx + log2f(sum) : -INFINITY,
-             idx == lo || idx - h * D == 0);
+        if (cp) {
+          cp_push(idx, sum > 0.0f ? o / sum : 0.0f, sum > 0.0f ? mx + log2f(sum) : -INFINITY);
+        } else {
+          emit(idx, h, sum > 0.0f ? o / sum : 0.0f, sum > 0.0f ? mx + log2f(sum) : -INFINITY,
+               idx == lo || idx - h * D == 0);
+        }
       }
       if (ctid == 0) {
         p.counters[counter] = 0;  // ready for the next call
@@ -738,9 +745,10 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
   }
-  if (cp && cid == 0) {
-    // ---- context parallel: CTA `rank` of cluster 0 merges slice `rank` of this kv
-    // head from every (rank, cluster) contribution, polling the tagged words ----
+  if (cp && (nclust == 1 || flags_s[1] != 0)) {
+    // ---- context parallel: the CTA that produced this rank's slice `rank` of the kv
+    // head merges that slice from every rank's contribution, polling the tagged
+    // words (one contribution per rank: its clusters are merged already) ----
     const int W = p.cp_world, par = cp_e & 1;
     const unsigned want = cp_e & 0xffffffu;
     const uint64_t dl = globaltimer_ns() + p.timeout_ns;
@@ -759,76 +767,36 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         o = o * sc + w * ov;
         mx = mn;
       };
-      // Contributions are read kBatch at a time, all loads of a batch in flight
-      // together; a batch is re-read until every tag is this call's. The first
-      // batch is the cluster-0 contribution of every rank, whose tag also gives that
-      // rank's cluster count; then the remaining (rank, cluster) pairs in order.
-      constexpr int kBatch = kMaxRanks;
-      int ncl[kMaxRanks];
+      // one contribution per rank; all of them are read together and re-read until
+      // every tag is this call's
+      uint2 wo[kMaxRanks], wl[kMaxRanks];
+      unsigned have = 0;  // bit r: rank r's words are this call's
+      const unsigned all = (1u << W) - 1u;
       bool ok = true;
-      int total = 0;
-      for (int j0 = 0; ok; j0 += kBatch) {
-        // pair j: j < W is (rank j, cluster 0); after that, (r, k >= 1) rank-major
-        int rr[kBatch], kk[kBatch];
-        int nb = 0;
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int j = j0 + u;
-          rr[u] = -1;
-          kk[u] = 0;
-          if (j0 == 0) {
-            if (j < W) {
-              rr[u] = j;
-              nb = u + 1;
-            }
-          } else if (j - W < total) {
-            int rest = j - W, r = 0;
-            while (r < W && rest >= ncl[r] - 1) {
-              rest -= ncl[r] - 1;
-              ++r;
-            }
-            rr[u] = r;
-            kk[u] = rest + 1;
-            nb = u + 1;
-          }
-        }
-        if (nb == 0) break;
-        uint2 wo[kBatch], wl[kBatch];
-        unsigned have = 0;  // bit u: pair u holds this call's words
 #pragma unroll 1
-        for (uint32_t it = 0;; ++it) {
+      for (uint32_t it = 0;; ++it) {
 #pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            if (u < nb && !(have & (1u << u))) {
-              const uint2* slot = cp_slot(p.cp_peer[p.cp_rank], par, rr[u], kk[u], W, p.Hkv, kvh, rank, cpw);
-              wo[u] = ld_word_sys(slot + (idx - lo));
-              wl[u] = ld_word_sys(slot + lw);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u)
-            if (u < nb && (wo[u].y >> 8) == want && (wl[u].y >> 8) == want) have |= 1u << u;
-          if (have == (1u << nb) - 1u) break;
-          if ((it & 15u) == 15u && globaltimer_ns() > dl) {
-            ok = false;
-            break;
-          }
-          __nanosleep(32);
-        }
-        if (!ok) break;
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          if (u < nb) {
-            fold(wo[u], wl[u]);
-            if (j0 == 0) ncl[u] = min(static_cast<int>(wo[u].y & 0xffu), kCpMaxClusters);
+        for (int r = 0; r < kMaxRanks; ++r) {
+          if (r < W && !(have & (1u << r))) {
+            const uint2* slot = cp_slot(p.cp_peer[p.cp_rank], par, r, W, p.Hkv, kvh, rank, cpw);
+            wo[r] = ld_word_sys(slot + (idx - lo));
+            wl[r] = ld_word_sys(slot + lw);
           }
         }
-        if (j0 == 0) {
-          total = 0;
-          for (int r = 0; r < W; ++r) total += max(ncl[r], 1) - 1;
-          // the (r, k >= 1) pairs start at j = W: continue from there
-          j0 = W - kBatch;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < W && (wo[r].y >> 8) == want && (wl[r].y >> 8) == want) have |= 1u << r;
+        if (have == all) break;
+        if ((it & 15u) == 15u && globaltimer_ns() > dl) {
+          ok = false;
+          break;
         }
+        __nanosleep(32);
+      }
+      if (ok) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < W) fold(wo[r], wl[r]);
       }
       if (ok && !aborted) {
         write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
@@ -839,8 +807,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (late) record_status(p.status, QIC_DEV_PEER_TIMEOUT);
     // the last slice merger of this call advances the epoch for the next call
     consumer_sync();
-    // every cluster of this rank's kv head has contributed: past every stage loop
-    if (nclust > 1 && rank == 0 && stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
     if (ctid == 0) {
       const unsigned prev = atomicAdd(p.cp_done, 1u);
       if (prev == static_cast<unsigned>(p.cp_mergers) - 1u) {

@@ -331,7 +331,6 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     int nclust = std::max(1, max_clusters / Hkv);
-    if (cp != nullptr) nclust = std::min(nclust, qic::kCpMaxClusters);
     n_splits = cluster * nclust;
     if (n_splits > n_stages) {
       nclust = std::max(1, n_stages / cluster);
@@ -346,9 +345,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
     cluster = n_splits;
   }
-  if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0 ||
-                        n_splits / qic::kCpSlices > qic::kCpMaxClusters))
-    return QIC_ERROR_NOT_SUPPORTED;
+  if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0)) return QIC_ERROR_NOT_SUPPORTED;
   const int n_clusters = n_splits / cluster;
   if (n_clusters > 1) {
     const size_t need = qic::kWsPartialOffset +

@@ -40,17 +40,16 @@ __host__ __device__ constexpr int partial_floats(int G, int D) { return ((G * (D
 constexpr size_t kWsCpEpoch = 64;
 constexpr size_t kWsCpDone = 128;
 constexpr int kMaxRanks = QIC_MAX_RANKS;
-constexpr int kCpSlices = 8;        // exchange slices per kv head: one per CTA of an 8-CTA cluster
-constexpr int kCpMaxClusters = 16;  // clusters per kv head on one rank in context-parallel launches
+constexpr int kCpSlices = 8;  // exchange slices per kv head: one per CTA of an 8-CTA cluster
 // Exchange words: 8 bytes, {fp32 value, tag}, written with one 8-byte store so a
 // reader that sees the tag sees the value (no fence, no separate flag). tag =
-// (epoch & 0xffffff) << 8 | clusters of the writing rank.
-// Exchange buffer of one rank: [2 parities][world sources][kCpMaxClusters][Hkv]
-// [kCpSlices] contributions of cp_slice_words words each: the slice's outputs, then
-// the log-sum-exp of the head of its first and of its last output.
+// (epoch & 0xffffff) << 8 | contributions of the writing rank (1).
+// Exchange buffer of one rank: [2 parities][world sources][Hkv][kCpSlices]
+// contributions of cp_slice_words words each: the slice's outputs, then the
+// log-sum-exp of the head of its first and of its last output.
 __host__ __device__ constexpr int cp_slice_words(int G, int D) { return (G * D + kCpSlices - 1) / kCpSlices + 2; }
 __host__ __device__ constexpr size_t cp_exchange_bytes(int G, int D, int Hkv, int world) {
-  return static_cast<size_t>(2) * world * kCpMaxClusters * Hkv * kCpSlices * cp_slice_words(G, D) * 8;
+  return static_cast<size_t>(2) * world * Hkv * kCpSlices * cp_slice_words(G, D) * 8;
 }
 
 // Work of one CTA in a planned (batched) launch: stages [st_lo, st_hi) of sequence b
