@@ -69,10 +69,15 @@ enum {
                                     values (log2 of the sum of 2^(score*log2(e)/sqrt(d))), padded to a
                                     multiple of 4 floats; no gate. Partials of disjoint token ranges
                                     of one sequence combine with qic_attention_merge. */
-  QIC_EXPLICIT_POSITION = 16     /* args->position is the token position used for RoPE of q and of the
+  QIC_EXPLICIT_POSITION = 16,    /* args->position is the token position used for RoPE of q and of the
                                     appended k (default seq_len-1). The append still writes the last
                                     attended row (index seq_len-1 of this call's cache or page table):
                                     a rank that holds the final shard of a longer sequence. */
+  QIC_DETERMINISTIC = 32         /* bitwise-reproducible outputs. Without it, single-sequence calls with
+                                    a workspace and at least 8 stages per split hand the first eighth
+                                    of the sequence's stages to whichever CTA asks first (load
+                                    balance), so the order in which split partials are summed, and the
+                                    last bits of the output, can change from call to call. */
 };
 
 const char* qic_status_string(int status);

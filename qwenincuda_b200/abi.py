@@ -16,6 +16,7 @@ QIC_DEV_BAD_PLAN = 8
 QIC_PDL = 4
 QIC_PARTIAL_OUT = 8
 QIC_EXPLICIT_POSITION = 16
+QIC_DETERMINISTIC = 32
 QIC_MAX_RANKS = 8
 QIC_IPC_HANDLE_BYTES = 64
 

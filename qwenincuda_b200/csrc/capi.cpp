@@ -360,7 +360,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
       p.counters = reinterpret_cast<int*>(ws + qic::kWsHeader);
       p.part = reinterpret_cast<float*>(ws + qic::kWsPartialOffset);
       p.num_counters = std::min(Hkv * cluster, qic::kMaxCounters - qic::kMaxStageCounters);
-      if (Hkv <= qic::kMaxStageCounters)
+      if (Hkv <= qic::kMaxStageCounters && !(a->flags & QIC_DETERMINISTIC))
         p.stage_ctr = p.counters + (qic::kMaxCounters - qic::kMaxStageCounters);
       p.part_slots = static_cast<int>(std::min<size_t>(
           INT32_MAX, (a->workspace_bytes - qic::kWsPartialOffset) / (qic::partial_floats(G, D) * sizeof(float))));

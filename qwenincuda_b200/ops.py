@@ -16,6 +16,7 @@ import torch
 from .abi import (
     QIC_DTYPE_BF16,
     QIC_DTYPE_F16,
+    QIC_DETERMINISTIC,
     QIC_EXPLICIT_POSITION,
     QIC_FUSE_APPEND,
     QIC_FUSE_Q_PROLOGUE,
@@ -105,10 +106,12 @@ def kv_append(k_new, v_new, k_norm_w, eps, rope_theta, position, k_cache, v_cach
 def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, seq_len, page_table=None,
                 page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
                 rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
-                cache_tokens=None, pdl=False, cluster_size=0, position=None, partial_out=False) -> DecodeArgs:
+                cache_tokens=None, pdl=False, cluster_size=0, position=None, partial_out=False,
+                deterministic=False) -> DecodeArgs:
     """qic_decode_args for one call. position: RoPE position of q and the appended k
     (default seq_len - 1). partial_out: `out` is an fp32 tensor of
-    num_kv_heads * partial_floats(...) elements receiving the (o, lse) partial."""
+    num_kv_heads * partial_floats(...) elements receiving the (o, lse) partial.
+    deterministic: bitwise-reproducible outputs (no dynamic stage pool)."""
     a = DecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads = num_heads
@@ -127,6 +130,8 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
     if position is not None:
         a.flags |= QIC_EXPLICIT_POSITION
         a.position = int(position)
+    if deterministic:
+        a.flags |= QIC_DETERMINISTIC
     if partial_out:
         if out.dtype != torch.float32:
             raise TypeError("a partial output is float32")

@@ -270,3 +270,26 @@ def test_stage_pool_counters_reset_between_calls():
     # the ticket counters (the last 64 counters) are back at zero
     top = w.buf[256 + (8192 - 64) * 4: 256 + 8192 * 4].view(torch.int32)
     assert int(top.abs().sum()) == 0
+
+
+def test_deterministic_flag_reproduces_bits():
+    """With QIC_DETERMINISTIC two calls give the same bits; without it (stage pool on,
+    33 stages per split here) every call stays within tolerance of the reference."""
+    H, Hkv, d, S, P = 32, 8, 128, 40001, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S, P, torch.bfloat16, seed=51)
+    want = _ref(qv, kc, vc, H, Hkv, d, S, table, P)
+    w = q.Workspace(H, Hkv, d, S)
+    outs = {}
+    for det in (True, False):
+        runs = []
+        for _ in range(3):
+            out = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+            q.decode_attention(q=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d,
+                               seq_len=S, page_table=table, page_size=P, workspace=w, deterministic=det)
+            torch.cuda.synchronize()
+            assert w.status() == 0
+            ok, err, idx = allclose_report(out, want, ATOL, RTOL)
+            assert ok, f"deterministic={det}: max abs err {err} at {idx}"
+            runs.append(out)
+        outs[det] = runs
+    assert all(torch.equal(r.view(torch.int16), outs[True][0].view(torch.int16)) for r in outs[True])

@@ -213,3 +213,70 @@ def test_cp_rejects_bad_arguments():
     a.cluster_size = 0
     a.workspace = None
     assert q.lib().qic_cp_decode_attention(ctypes.byref(a), ctypes.byref(args), stream) == 1
+
+
+def _gated_case(S, seed, dtype=torch.bfloat16):
+    """Qwen3.5 gated-attention shape (16 q heads, 4 kv heads, d=256): paged cache,
+    raw q / k_new / v_new, norm weights and the output gate."""
+    Hg, Hkvg, Dg = 16, 4, 256
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    pages = (S + P - 1) // P
+    kc = (torch.randn(pages * P, Hkvg * Dg, generator=g, device="cuda") * 0.5).to(dtype)
+    vc = (torch.randn(pages * P, Hkvg * Dg, generator=g, device="cuda") * 0.5).to(dtype)
+    tab = torch.randperm(pages, generator=g, device="cuda").to(torch.int32)
+    qv = torch.randn(Hg * Dg, generator=g, device="cuda").to(dtype)
+    kn = torch.randn(Hkvg * Dg, generator=g, device="cuda").to(dtype)
+    vn = (torch.randn(Hkvg * Dg, generator=g, device="cuda") * 0.5).to(dtype)
+    gate = torch.randn(Hg * Dg, generator=g, device="cuda").to(dtype)
+    w = (1.0 + 0.1 * torch.randn(Dg, generator=g, device="cuda")).to(dtype)
+    kw = dict(q=qv, k_cache=kc, v_cache=vc, num_heads=Hg, num_kv_heads=Hkvg, head_dim=Dg, seq_len=S,
+              page_table=tab, page_size=P, q_norm_w=w, k_norm_w=w, k_new=kn, v_new=vn, fuse_q=True, gate=gate)
+    return (Hg, Hkvg, Dg), kw
+
+
+def test_fused_exchange_world1_gated_d256():
+    """Gated d=256 shape through the fused exchange at world 1: bit-identical to the
+    plain call (gate applied once, after the merge), two calls in a row. Both run with
+    QIC_DETERMINISTIC: at this length the stage pool would otherwise change the order
+    of the split sums from call to call."""
+    S = 16385
+    (Hg, Hkvg, Dg), kw = _gated_case(S, seed=41)
+    group = cpm.ExchangeGroup(Hg, Hkvg, Dg, rank=0, world=1, gather=lambda b, r, n: [b])
+    try:
+        ws_cp = q.Workspace(Hg, Hkvg, Dg, S)
+        ws = q.Workspace(Hg, Hkvg, Dg, S)
+        for call in range(2):
+            out_cp = torch.full((Hg * Dg,), float("nan"), device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(Hg * Dg, device="cuda", dtype=torch.bfloat16)
+            cpm.cp_decode_attention(group, out=out_cp, workspace=ws_cp, position=S - 1, cluster_size=8,
+                                    deterministic=True, **kw)
+            q.decode_attention(out=out, workspace=ws, cluster_size=8, deterministic=True, **kw)
+            torch.cuda.synchronize()
+            assert ws_cp.status() == 0 and ws.status() == 0
+            assert torch.equal(out_cp.view(torch.int16), out.view(torch.int16)), f"call {call}"
+    finally:
+        torch.cuda.synchronize()
+        group.close()
+
+
+def test_gated_d256_partials_merge_with_gate():
+    """Gated d=256 shape: two token ranges as partials (q prologue at the global
+    position), merged with the gate by qic_attention_merge, equal the whole call."""
+    S = 6001
+    (Hg, Hkvg, Dg), kw = _gated_case(S, seed=43)
+    gate = kw.pop("gate")
+    ref = torch.empty(Hg * Dg, device="cuda", dtype=torch.bfloat16)
+    q.decode_attention(out=ref, gate=gate, workspace=q.Workspace(Hg, Hkvg, Dg, S), **kw)
+    pf = q.ops.partial_floats(Hg, Hkvg, Dg)
+    parts = torch.empty((2, Hkvg * pf), device="cuda", dtype=torch.float32)
+    tab = kw["page_table"]
+    cut = 200 * P  # tokens [0, cut) and [cut, S): the second range's table is the tail of the first
+    for r, (t0, t1) in enumerate([(0, cut), (cut, S)]):
+        kr = dict(kw, seq_len=t1 - t0, page_table=tab[t0 // P:].contiguous())
+        q.decode_attention(out=parts[r], workspace=q.Workspace(Hg, Hkvg, Dg, t1 - t0), position=S - 1,
+                           partial_out=True, **kr)
+    out = torch.empty(Hg * Dg, device="cuda", dtype=torch.bfloat16)
+    q.ops.attention_merge(parts, Hg, Hkvg, Dg, out, gate=gate)
+    torch.cuda.synchronize()
+    ok, err, idx = allclose_report(out, ref, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
