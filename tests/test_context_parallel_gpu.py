@@ -122,9 +122,10 @@ def test_partial_out_single_split_and_gate():
     assert ok, f"max abs err {err} at {idx}"
 
 
-def test_fused_exchange_world1_equals_plain_call():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_exchange_world1_equals_plain_call(dtype):
     S = 8192
-    k, v, qv, kn, vn, w = _sequence(S, seed=21)
+    k, v, qv, kn, vn, w = _sequence(S, seed=21, dtype=dtype)
     kc, tab = _paged(k, seed=5)
     vc, _ = _paged(v, seed=5)
     group = cpm.ExchangeGroup(H, HKV, D, rank=0, world=1, gather=lambda b, r, n: [b])
