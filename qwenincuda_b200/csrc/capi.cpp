@@ -327,9 +327,14 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   if (n_splits <= 0) {
     // As many CTAs as can be resident in one wave: clusters of 8 (measured best on B200),
     // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
+    // With programmatic dependent launch (layers chained back to back) a sixth of the
+    // resident slots is left free, so the next launch's CTAs start their copies while
+    // this one merges its splits (measured on 36 chained S=8192 layers: 13.6 -> 12.8
+    // us per layer; 8 chained d=256 S=32769 layers: 31.3 -> 30.2 us).
     if (cluster == 0) cluster = 8;
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
+    if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
     int nclust = std::max(1, max_clusters / Hkv);
     n_splits = cluster * nclust;
     if (n_splits > n_stages) {
