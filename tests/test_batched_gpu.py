@@ -85,7 +85,9 @@ def test_batched_fused_append_and_oracle(oracle):
 
 def test_pdl_chain_matches_plain_launches():
     """Back-to-back calls with programmatic dependent launch give the same bytes as
-    plain launches (the second call reads the first call's output as its q)."""
+    plain launches (the second call reads the first call's output as its q). Both use
+    the same split shape: by default chained launches leave a sixth of the resident
+    slots free and so split differently."""
     from qwenincuda_b200.workloads import AttnConfig, make_attention_inputs
 
     cfg = AttnConfig("pdl", 32, 8, 128, 3000, layers=4, seed=9)
@@ -100,7 +102,7 @@ def test_pdl_chain_matches_plain_launches():
                                num_heads=32, num_kv_heads=8, head_dim=128, seq_len=cfg.seq_len,
                                page_table=inp.page_table[layer], page_size=16, q_norm_w=inp.q_norm_w,
                                k_norm_w=inp.k_norm_w, k_new=inp.k_new[layer], v_new=inp.v_new[layer], fuse_q=True,
-                               fuse_append=True, workspace=ws, pdl=pdl)
+                               fuse_append=True, workspace=ws, pdl=pdl, num_splits=40, cluster_size=8)
         torch.cuda.synchronize()
         assert ws.status() == 0
         outs.append((inp.out.clone(), inp.k_cache.clone()))
