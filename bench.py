@@ -514,6 +514,8 @@ def cpu_baseline(cfg, budget_s=6.0):
     from qwenincuda_b200.workloads import make_attention_inputs
 
     orc = Oracle()
+    # every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    orc.set_num_threads(len(os.sched_getaffinity(0)))
     threads = orc.num_threads()
     inp = make_attention_inputs(cfg, paged=True, layers=1, device="cpu")
     H, Hkv, d, S = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len
