@@ -495,7 +495,30 @@ int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv
         std::min<double>(max_waves, std::max(1.0, std::round(bytes / (static_cast<double>(resident) * (1 << 20))))));
     target_ctas = resident * waves;
   }
-  const long long chunk = std::max<long long>(1, (total + target_ctas - 1) / target_ctas);
+  // stages per item: the smallest chunk whose item count (every (sequence, kv head)
+  // cut into pieces of at most `chunk` stages, ragged last pieces included) fits the
+  // target, so the ragged pieces do not spill into a nearly empty extra wave
+  long long chunk = std::max<long long>(1, (total + target_ctas - 1) / target_ctas);
+  auto items_for = [&](long long c) {
+    long long n_items = 0;
+    for (int b = 0; b < batch; ++b) {
+      const long long n = (seq_lens[b] + tok - 1) / tok;
+      n_items += std::min<long long>(std::min<long long>(n, qic::kMaxSplits), (n + c - 1) / c) * num_kv_heads;
+    }
+    return n_items;
+  };
+  if (items_for(chunk) > target_ctas) {
+    // items_for falls as the chunk grows; at the longest sequence's stage count every
+    // (sequence, kv head) is one item, the fewest possible
+    long long lo = chunk, hi = 1;
+    for (int b = 0; b < batch; ++b) hi = std::max<long long>(hi, (seq_lens[b] + tok - 1) / tok);
+    hi = std::max(hi, lo);
+    while (lo < hi) {
+      const long long mid = lo + (hi - lo) / 2;
+      if (items_for(mid) > target_ctas) lo = mid + 1; else hi = mid;
+    }
+    chunk = lo;
+  }
   std::vector<qic::WorkItem> out;
   int part_base = 0;
   for (int b = 0; b < batch; ++b) {
