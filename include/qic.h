@@ -149,7 +149,11 @@ typedef struct qic_decode_args {
   int64_t position;         /* QIC_EXPLICIT_POSITION: RoPE position of q and the appended k */
 } qic_decode_args;
 
-/* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len). */
+/* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len).
+ * A workspace holds the status word, merge and stage-ticket counters, split partials
+ * and (context parallel) the call epoch: calls that may run at the same time on the
+ * GPU (different streams) need different workspaces; calls in stream order may share
+ * one, whatever their shapes. Every call leaves the counters at zero. */
 size_t qic_decode_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int max_seq_len);
 
 /* Zeroes a workspace (counters and the device status word). Call once after allocating it. */
