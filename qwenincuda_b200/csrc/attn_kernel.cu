@@ -870,15 +870,6 @@ cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partial
 // ----------------------------------------------------------------------------
 // host launcher
 // ----------------------------------------------------------------------------
-size_t decode_attention_smem_bytes(int head_dim) {
-  switch (head_dim) {
-    case 64: return AttnShape<64>::kSmemBytes;
-    case 128: return AttnShape<128>::kSmemBytes;
-    case 256: return AttnShape<256>::kSmemBytes;
-    default: return 0;
-  }
-}
-
 template <typename T, int D>
 static cudaError_t configure_typed() {
   static unsigned long long configured = 0;  // one bit per device ordinal

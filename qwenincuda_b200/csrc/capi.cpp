@@ -73,8 +73,6 @@ uint64_t timeout_ns() {
   return t;
 }
 
-size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-
 // Bytes of the allocation containing `p` from p to its end, 0 if unknown.
 size_t bytes_to_allocation_end(const void* p) {
   load_driver_entry_points();

@@ -106,7 +106,6 @@ struct AttnParams {
 
 // Launchers (attn_kernel.cu)
 cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream);
-size_t decode_attention_smem_bytes(int head_dim);
 // out = log-sum-exp merge of n partials [n][Hkv][partial_floats] (+ gate)
 cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partials, int n, int H, int Hkv,
                                    const void* gate, void* out, cudaStream_t stream);
