@@ -280,6 +280,7 @@ def gdn_workload():
     g.dtype = 1
     g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
     g.conv_kernel, g.eps = cfg.conv_kernel, cfg.eps
+    g.flags = q.abi.QIC_PDL  # the layer after it may start its copies while it runs
     for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state", "out"):
         setattr(g, k, t[k].data_ptr())
     step = _call(q.lib().qic_gated_delta_decode, g)

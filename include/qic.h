@@ -306,7 +306,9 @@ typedef struct qic_gdn_args {
   int32_t v_head_dim;       /* dv == 128 */
   int32_t conv_kernel;      /* K in [1, 8] */
   float eps;                /* gated RMSNorm epsilon */
-  int32_t reserved;
+  uint32_t flags;           /* QIC_PDL: may start while the previous kernel in the stream runs;
+                               every input and the state are read after it has completed. The
+                               kernel always lets the next kernel in the stream start early. */
   const void* qkv;          /* [2*Hk*dk + Hv*dv] in_proj_qkv output (conv input) */
   const void* z;            /* [Hv*dv] */
   const void* b;            /* [Hv] */

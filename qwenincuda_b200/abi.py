@@ -142,7 +142,7 @@ class GdnArgs(ctypes.Structure):
         ("v_head_dim", ctypes.c_int32),
         ("conv_kernel", ctypes.c_int32),
         ("eps", ctypes.c_float),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
         ("qkv", ctypes.c_void_p),
         ("z", ctypes.c_void_p),
         ("b", ctypes.c_void_p),

@@ -42,6 +42,11 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   constexpr int RPT = kGdnDk / RG;           // rows per thread
   static_assert(RPT * RG == kGdnDk, "row split");
 
+  // the next kernel in the stream may start (its own griddepcontrol.wait keeps it
+  // from reading this kernel's outputs early); this kernel reads its inputs and the
+  // state only after the kernel before it has completed
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int vloc = rank / CB;
@@ -267,13 +272,15 @@ static cudaError_t launch_gdn_typed(const qic_gdn_args& a, cudaStream_t stream) 
   cfg.blockDim = dim3(kGdnThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = REP * CB;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = (a.flags & QIC_PDL) ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gated_delta_kernel<T, REP, CB>, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -190,9 +190,10 @@ def launch_paged_attention(q, k_cache, v_cache, page_table, page_size, num_heads
 
 def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, out,
                        num_k_heads, num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6,
-                       stream=None):
+                       pdl=False, stream=None):
     """One GatedDeltaNet decode step; conv_state and recurrent_state (fp32) are updated in place."""
     g = GdnArgs()
+    g.flags = QIC_PDL if pdl else 0
     g.dtype = dtype_code(qkv)
     g.num_k_heads = num_k_heads
     g.num_v_heads = num_v_heads
