@@ -218,19 +218,23 @@ def attention_workload(name, layout, layers=None):
     inp = make_attention_inputs(cfg, paged=(layout == "paged"), layers=layers)
     L_ = inp.q.shape[0]
     # the step's per-layer inputs (q, k_new, v_new of every layer) live in one device
-    # buffer, so the end-to-end step moves them with one host-to-device copy
-    packed, views = _pack([inp.q, inp.k_new, inp.v_new])
-    inp.q, inp.k_new, inp.v_new = views
+    # buffer, so the end-to-end step moves them with one host-to-device copy. Gated
+    # layers take q as the interleaved [H, 2d] q/gate projection (the output of the
+    # reference's wq GEMV, src/model.cpp:627), so the gate moves with it.
+    gated = inp.gate is not None
+    qin = torch.cat([inp.q, inp.gate], dim=2) if gated else inp.q
+    packed, views = _pack([qin, inp.k_new, inp.v_new])
+    qin, inp.k_new, inp.v_new = views
     ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len)
     fns = []
     for layer in range(L_):
         a = q.ops.decode_args(
-            q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=inp.out[layer],
+            q=qin[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=inp.out[layer],
             num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
             page_table=inp.page_table[layer] if inp.paged else None, page_size=cfg.page_size,
-            gate=None if inp.gate is None else inp.gate[layer], q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w,
-            k_new=inp.k_new[layer], v_new=inp.v_new[layer], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True,
-            fuse_append=True, workspace=ws, cache_tokens=inp.cache_tokens, pdl=True)
+            q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w, k_new=inp.k_new[layer], v_new=inp.v_new[layer],
+            eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True, fuse_append=True, workspace=ws,
+            cache_tokens=inp.cache_tokens, pdl=True, q_gate_interleaved=gated)
         fns.append(_call(q.lib().qic_decode_attention, a))
 
     def step():
@@ -251,7 +255,7 @@ def attention_workload(name, layout, layers=None):
                 kernel="decode_attn_kernel", status=ws.status, keep=(inp, ws, packed),
                 config={"layout": layout, "page_size": cfg.page_size, "layers": L_, "seq_len": cfg.seq_len,
                         "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
-                        "gate": cfg.gate})
+                        "gate": "interleaved q/gate projection" if gated else False})
 
 
 def _pack(tensors):
@@ -544,8 +548,9 @@ def cpu_baseline(cfg, budget_s=6.0):
 def reference_gpu(cfg, layers, steps, warmup):
     """The reference's own kernels (src/kernels.cu built for sm_100a with
     --use_fast_math, bf16 instance) driving the per-layer sequence of
-    src/model.cpp:633-650: head-norm q and k, RoPE q and k, two row copies, paged
-    attention."""
+    src/model.cpp:628-650: (gated layers) split of the q/gate projection, head-norm
+    q and k, RoPE q and k, two row copies, paged attention, (gated layers) the
+    sigmoid gate."""
     from oracle.oracle import RefKernels, _p
     from qwenincuda_b200.workloads import make_attention_inputs
 
@@ -555,12 +560,17 @@ def reference_gpu(cfg, layers, steps, warmup):
     H, Hkv, d, S, P, pos = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len, cfg.page_size, cfg.position
     lib = ref.lib
     qbuf = torch.empty(H * d, device="cuda", dtype=dtype)
+    gbuf = torch.empty(H * d, device="cuda", dtype=dtype)
     kbuf = torch.empty(Hkv * d, device="cuda", dtype=dtype)
     slots = [int(inp.page_table[i][pos // P]) * P + pos % P for i in range(layers)]
+    qg = torch.cat([inp.q, inp.gate], dim=2).contiguous() if inp.gate is not None else None
 
     def step():
         for i in range(layers):
-            qbuf.copy_(inp.q[i].flatten())
+            if qg is not None:
+                lib.qicref_split_q_gate(_p(qg[i]), H, d, _p(qbuf), _p(gbuf))
+            else:
+                qbuf.copy_(inp.q[i].flatten())
             kbuf.copy_(inp.k_new[i].flatten())
             lib.qicref_head_rmsnorm(_p(qbuf), _p(inp.q_norm_w), H, d, cfg.eps, _p(qbuf))
             lib.qicref_head_rmsnorm(_p(kbuf), _p(inp.k_norm_w), Hkv, d, cfg.eps, _p(kbuf))
@@ -572,6 +582,8 @@ def reference_gpu(cfg, layers, steps, warmup):
             lib.qicref_copy_row(_p(vc), _p(inp.v_new[i].flatten()), slots[i], Hkv * d)
             lib.qicref_paged_attention(_p(qbuf), _p(kc), _p(vc), _p(inp.page_table[i]), P, H, Hkv, d, S,
                                        _p(inp.out[i]))
+            if qg is not None:
+                lib.qicref_sigmoid_mul_inplace(_p(inp.out[i]), _p(gbuf), H * d)
 
     for _ in range(warmup):
         step()

@@ -73,11 +73,16 @@ enum {
                                     appended k (default seq_len-1). The append still writes the last
                                     attended row (index seq_len-1 of this call's cache or page table):
                                     a rank that holds the final shard of a longer sequence. */
-  QIC_DETERMINISTIC = 32         /* bitwise-reproducible outputs. Without it, single-sequence calls with
+  QIC_DETERMINISTIC = 32,        /* bitwise-reproducible outputs. Without it, single-sequence calls with
                                     a workspace and at least 8 stages per split hand the first eighth
                                     of the sequence's stages to whichever CTA asks first (load
                                     balance), so the order in which split partials are summed, and the
                                     last bits of the output, can change from call to call. */
+  QIC_Q_GATE_INTERLEAVED = 64    /* q is the interleaved q/gate projection [H, 2d] (per head d q values,
+                                    then d gate values) and out *= sigmoid(gate) with that gate; `gate`
+                                    must be NULL. Folds launch_split_q_gate_interleaved
+                                    (src/kernels.cu:113-127, src/model.cpp:628) into the kernel. Batched
+                                    calls: q is [B, H, 2d]. Partial outputs carry no gate. */
 };
 
 const char* qic_status_string(int status);

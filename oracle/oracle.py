@@ -147,6 +147,7 @@ class RefKernels:
         lib.qicref_head_rmsnorm.argtypes = [_vp, _vp, _i, _i, _f, _vp]
         lib.qicref_rope_inplace.argtypes = [_vp, _i, _i, _i, _f]
         lib.qicref_sigmoid_mul_inplace.argtypes = [_vp, _vp, _i]
+        lib.qicref_split_q_gate.argtypes = [_vp, _i, _i, _vp, _vp]
         lib.qicref_flash_attention.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _vp]
         lib.qicref_paged_attention.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]
         lib.qicref_copy_row.argtypes = [_vp, _vp, ctypes.c_longlong, _i]
@@ -178,6 +179,11 @@ class RefKernels:
     def sigmoid_mul_inplace(self, x, gate, n):
         torch.cuda.synchronize()
         self._chk(self.lib.qicref_sigmoid_mul_inplace(_p(x), _p(gate), n), "sigmoid_mul")
+        self.sync()
+
+    def split_q_gate(self, packed, num_heads, head_dim, q, gate):
+        torch.cuda.synchronize()
+        self._chk(self.lib.qicref_split_q_gate(_p(packed), num_heads, head_dim, _p(q), _p(gate)), "split_q_gate")
         self.sync()
 
     def flash_attention(self, q, k_cache, v_cache, num_heads, num_kv_heads, head_dim, seq_len, ctx, sync=True):

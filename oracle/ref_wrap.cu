@@ -25,6 +25,12 @@ int qicref_sigmoid_mul_inplace(void* x, const void* gate, int n) {
   return static_cast<int>(cudaGetLastError());
 }
 
+int qicref_split_q_gate(const void* packed, int num_heads, int head_dim, void* q, void* gate) {
+  launch_split_q_gate_interleaved(static_cast<const half*>(packed), num_heads, head_dim, static_cast<half*>(q),
+                                  static_cast<half*>(gate));
+  return static_cast<int>(cudaGetLastError());
+}
+
 int qicref_flash_attention(const void* q, const void* k, const void* v, int num_heads, int num_kv_heads,
                            int head_dim, int seq_len, void* ctx) {
   launch_flash_attention(static_cast<const half*>(q), static_cast<const half*>(k), static_cast<const half*>(v),

@@ -17,6 +17,7 @@ QIC_PDL = 4
 QIC_PARTIAL_OUT = 8
 QIC_EXPLICIT_POSITION = 16
 QIC_DETERMINISTIC = 32
+QIC_Q_GATE_INTERLEAVED = 64
 QIC_MAX_RANKS = 8
 QIC_IPC_HANDLE_BYTES = 64
 

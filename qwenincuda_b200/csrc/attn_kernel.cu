@@ -92,12 +92,12 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* addr, int v) {
   return old;
 }
 
-// out = T(o), then the optional sigmoid gate as the reference applies it.
+// out[i] = T(o), then the optional sigmoid gate gate[gi] as the reference applies it.
 template <typename T>
-__device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, float o) {
+__device__ __forceinline__ void write_out(T* ob, const T* gb, size_t i, size_t gi, float o) {
   T ot = from_f32<T>(o);
   if (gb != nullptr) {
-    const float g = to_f32<T>(gb[i]);
+    const float g = to_f32<T>(gb[gi]);
     const float sig = 1.0f / (1.0f + expf(-g));
     ot = from_f32<T>(to_f32<T>(ot) * sig);
   }
@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int hd = p.head_dim;
   const T* qb = static_cast<const T*>(p.q) + static_cast<size_t>(b) * p.q_bstride;
   const T* gb = p.gate != nullptr ? static_cast<const T*>(p.gate) + static_cast<size_t>(b) * p.q_bstride : nullptr;
-  T* ob = static_cast<T*>(p.out) + static_cast<size_t>(b) * p.q_bstride;
+  T* ob = static_cast<T*>(p.out) + static_cast<size_t>(b) * p.out_bstride;
+  const int qhs = p.q_hstride;  // D, or 2D for the interleaved q/gate projection
   // RoPE position of q and of the appended k: the last attended token, or the
   // caller's global position when this launch holds one shard of a longer sequence
   const int rpos = (p.plan == nullptr && p.rope_pos >= 0) ? static_cast<int>(p.rope_pos) : S - 1;
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     for (int r = warp; r < nrows; r += kConsumerWarps) {
       float v[D / 32];
       if (r < G) {
-        row_load<T, D>(qb + static_cast<size_t>(kvh * G + r) * D, v, lane);
+        row_load<T, D>(qb + static_cast<size_t>(kvh * G + r) * qhs, v, lane);
         if (p.flags & QIC_FUSE_Q_PROLOGUE) {
           row_rmsnorm<T, D>(v, static_cast<const T*>(p.q_norm_w), hd, p.eps, lane);
           row_rope<T, D>(v, hd, rpos, p.theta, lane);
@@ -595,6 +596,10 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   }
   consumer_sync();
   const size_t qoff = static_cast<size_t>(kvh) * G * D;  // first output row of this group
+  // gate element of output idx of this group (head idx / D, dim idx % D)
+  auto gidx = [&](int idx) -> size_t {
+    return static_cast<size_t>(kvh * G + idx / D) * qhs + (idx % D);
+  };
   const int GD = G * D;
   const int pf = partial_floats(G, D);
   constexpr bool cp = CP;
@@ -607,7 +612,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       po[idx] = o;
       if (head_first) po[GD + h] = lse;
     } else {
-      write_out<T>(ob, gb, qoff + idx, o);
+      write_out<T>(ob, gb, qoff + idx, gidx(idx), o);
     }
   };
   if (!aborted) {
@@ -799,7 +804,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
           if (r < W) fold(wo[r], wl[r]);
       }
       if (ok && !aborted) {
-        write_out<T>(ob, gb, qoff + idx, sum > 0.0f ? o / sum : 0.0f);
+        write_out<T>(ob, gb, qoff + idx, gidx(idx), sum > 0.0f ? o / sum : 0.0f);
       } else if (!ok) {
         late = true;
       }
@@ -837,7 +842,7 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const float* __rest
     sum += w;
     o += w * pk[hh * D + d];
   }
-  write_out<T>(out, gate, static_cast<size_t>(i), sum > 0.0f ? o / sum : 0.0f);
+  write_out<T>(out, gate, static_cast<size_t>(i), static_cast<size_t>(i), sum > 0.0f ? o / sum : 0.0f);
 }
 
 template <typename T, int D>

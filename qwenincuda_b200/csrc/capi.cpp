@@ -208,6 +208,7 @@ int check_attention_common(int dtype, int H, int Hkv, int D, uint32_t flags, con
   const bool fuse_app = (flags & QIC_FUSE_APPEND) != 0;
   if (fuse_q && !q_norm_w) return QIC_ERROR_INVALID_VALUE;
   if (fuse_app && (!k_new || !v_new || !k_norm_w)) return QIC_ERROR_INVALID_VALUE;
+  if ((flags & QIC_Q_GATE_INTERLEAVED) && gate) return QIC_ERROR_INVALID_VALUE;  // the gate is inside q
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned2(out) || (gate && !aligned2(gate)) ||
       (fuse_q && !aligned16(q_norm_w)) ||
       (fuse_app && (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_norm_w))) ||
@@ -219,8 +220,12 @@ int check_attention_common(int dtype, int H, int Hkv, int D, uint32_t flags, con
 void fill_common(qic::AttnParams& p, int H, int Hkv, int D, const void* q, const void* gate, void* out,
                  void* k_cache, void* v_cache, uint32_t flags, float eps, float theta, const void* q_norm_w,
                  const void* k_norm_w, const void* k_new, const void* v_new) {
+  const bool interleaved = (flags & QIC_Q_GATE_INTERLEAVED) != 0;
   p.q = q;
-  p.gate = gate;
+  p.gate = interleaved ? static_cast<const void*>(static_cast<const char*>(q) + static_cast<size_t>(D) * 2) : gate;
+  p.q_hstride = interleaved ? 2 * D : D;
+  p.q_bstride = static_cast<long long>(H) * p.q_hstride;
+  p.out_bstride = static_cast<long long>(H) * D;
   p.out = out;
   p.k_cache = k_cache;
   p.v_cache = v_cache;
@@ -587,7 +592,6 @@ int qic_batch_decode_attention(const qic_batch_decode_args* a, qic_stream_t stre
               a->q_norm_w, a->k_norm_w, a->k_new, a->v_new);
   p.page_table = a->block_tables;
   p.table_bstride = a->max_pages_per_seq;
-  p.q_bstride = static_cast<long long>(H) * D;
   p.kv_new_bstride = static_cast<long long>(Hkv) * D;
   p.plan = static_cast<const qic::WorkItem*>(a->plan);
   p.cache_tokens = a->cache_tokens;

@@ -63,8 +63,8 @@ struct WorkItem {
 struct AttnParams {
   CUtensorMap tm_k;                  // 2D map over [tokens, kv_dim], box {64, box_h}, 128B swizzle
   CUtensorMap tm_v;
-  const void* q;                     // [H, D]
-  const void* gate;                  // [H, D] or null
+  const void* q;                     // [H, q_hstride]
+  const void* gate;                  // [H, q_hstride] or null
   void* out;                         // [H, D]
   void* k_cache;                     // generic pointers for the fused append
   void* v_cache;
@@ -77,7 +77,9 @@ struct AttnParams {
   int* counters;                     // one merge counter per (sequence, kv head)
   int* status;                       // device status word
   const WorkItem* plan;              // null: one sequence, grid (n_splits, Hkv)
-  long long q_bstride;               // elements between sequences in q / out / gate
+  long long q_bstride;               // elements between sequences in q / gate
+  long long out_bstride;             // elements between sequences in out
+  int q_hstride;                     // elements between heads in q / gate: D, or 2D when interleaved
   long long kv_new_bstride;          // elements between sequences in k_new / v_new
   int table_bstride;                 // entries between sequences' block-table rows
   int part_slots;                    // partial slots available in the workspace

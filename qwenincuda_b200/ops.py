@@ -23,6 +23,7 @@ from .abi import (
     QIC_PARTIAL_OUT,
     QIC_PDL,
     QIC_PLAN_ITEM_BYTES,
+    QIC_Q_GATE_INTERLEAVED,
     BatchDecodeArgs,
     DecodeArgs,
     GdnArgs,
@@ -107,11 +108,13 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
                 page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
                 rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
                 cache_tokens=None, pdl=False, cluster_size=0, position=None, partial_out=False,
-                deterministic=False) -> DecodeArgs:
+                deterministic=False, q_gate_interleaved=False) -> DecodeArgs:
     """qic_decode_args for one call. position: RoPE position of q and the appended k
     (default seq_len - 1). partial_out: `out` is an fp32 tensor of
     num_kv_heads * partial_floats(...) elements receiving the (o, lse) partial.
-    deterministic: bitwise-reproducible outputs (no dynamic stage pool)."""
+    deterministic: bitwise-reproducible outputs (no dynamic stage pool).
+    q_gate_interleaved: q is the [H, 2d] q/gate projection and out is gated by its
+    second halves (gate must be None)."""
     a = DecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads = num_heads
@@ -126,7 +129,7 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
     a.page_table = _ptr(page_table)
     a.gate = _ptr(gate)
     a.out = _ptr(out)
-    a.flags = _flags(fuse_q, fuse_append, pdl)
+    a.flags = _flags(fuse_q, fuse_append, pdl, q_gate_interleaved)
     if position is not None:
         a.flags |= QIC_EXPLICIT_POSITION
         a.position = int(position)
@@ -150,8 +153,9 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
     return a
 
 
-def _flags(fuse_q, fuse_append, pdl):
-    return (QIC_FUSE_Q_PROLOGUE if fuse_q else 0) | (QIC_FUSE_APPEND if fuse_append else 0) | (QIC_PDL if pdl else 0)
+def _flags(fuse_q, fuse_append, pdl, q_gate_interleaved=False):
+    return ((QIC_FUSE_Q_PROLOGUE if fuse_q else 0) | (QIC_FUSE_APPEND if fuse_append else 0) |
+            (QIC_PDL if pdl else 0) | (QIC_Q_GATE_INTERLEAVED if q_gate_interleaved else 0))
 
 
 def decode_attention(stream=None, **kw):
@@ -238,7 +242,8 @@ class BatchPlan:
 
 def batch_decode_args(*, plan: BatchPlan, q, k_cache, v_cache, block_tables, out, num_heads, num_kv_heads, head_dim,
                       page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
-                      rope_theta=1.0e6, fuse_q=False, fuse_append=False, pdl=False, cache_tokens=None):
+                      rope_theta=1.0e6, fuse_q=False, fuse_append=False, pdl=False, cache_tokens=None,
+                      q_gate_interleaved=False):
     a = BatchDecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads, a.num_kv_heads, a.head_dim = num_heads, num_kv_heads, head_dim
@@ -246,7 +251,7 @@ def batch_decode_args(*, plan: BatchPlan, q, k_cache, v_cache, block_tables, out
     a.page_size = page_size
     a.cache_tokens = cache_tokens if cache_tokens is not None else k_cache.numel() // (num_kv_heads * head_dim)
     a.max_pages_per_seq = block_tables.shape[1]
-    a.flags = _flags(fuse_q, fuse_append, pdl)
+    a.flags = _flags(fuse_q, fuse_append, pdl, q_gate_interleaved)
     a.q, a.k_cache, a.v_cache = _ptr(q), _ptr(k_cache), _ptr(v_cache)
     a.block_tables, a.gate, a.out = _ptr(block_tables), _ptr(gate), _ptr(out)
     a.eps, a.rope_theta = eps, rope_theta

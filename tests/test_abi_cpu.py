@@ -99,6 +99,25 @@ def test_argument_validation_without_device():
     g.dtype, g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim, g.conv_kernel = 1, 16, 32, 64, 128, 4
     assert L.qic_gated_delta_decode(ctypes.byref(g), None) == 2
     assert L.qic_kv_append(1, None, None, None, 1e-6, 1e6, 0, None, None, None, 16, 10, 8, 128, None) == 1
+    a.seq_len = 10
+    a.flags = q.abi.QIC_Q_GATE_INTERLEAVED
+    a.gate = 0x30000
+    assert L.qic_decode_attention(ctypes.byref(a), None) == 1          # gate given twice (interleaved q)
+
+
+def test_header_constants_match_bindings():
+    """Every QIC_* enum value of include/qic.h has the same value in the ctypes bindings."""
+    from qwenincuda_b200 import abi
+
+    text = (ROOT / "include" / "qic.h").read_text()
+    consts = dict(re.findall(r"\b(QIC_[A-Z0-9_]+)\s*=\s*(\d+)", text))
+    consts.update(re.findall(r"#define\s+(QIC_[A-Z0-9_]+)\s+(\d+)", text))
+    assert len(consts) >= 20
+    for name, value in consts.items():
+        if name.startswith("QIC_ERROR_") or name == "QIC_SUCCESS":
+            assert abi.STATUS_NAMES[int(value)] == name
+        else:
+            assert getattr(abi, name) == int(value), name
 
 
 def test_libraries_bind_their_own_symbols():

@@ -293,3 +293,55 @@ def test_deterministic_flag_reproduces_bits():
             runs.append(out)
         outs[det] = runs
     assert all(torch.equal(r.view(torch.int16), outs[True][0].view(torch.int16)) for r in outs[True])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("paged", [True, False])
+def test_interleaved_q_gate_matches_reference_split(dtype, paged):
+    """QIC_Q_GATE_INTERLEAVED reads q and the output gate straight from the packed
+    [H, 2d] q/gate projection. The reference splits it with
+    launch_split_q_gate_interleaved (src/kernels.cu:113-127), then head-norms and
+    ropes q, attends and gates (src/model.cpp:628,633,636,644-650). The result is
+    also bit-identical to this library's call on the split q and gate."""
+    H, Hkv, d, S, P = 16, 4, 256, 4097, 16
+    eps, theta = 1e-6, 1.0e7
+    _, kc, vc, table = _inputs(H, Hkv, d, S, P, dtype, seed=61)
+    table = table if paged else None
+    g = _gen(62)
+    packed = torch.randn(H * 2 * d, generator=g, device="cuda").to(dtype)
+    qnw = (1.0 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(dtype)
+    ref = RefKernels(dtype)
+    qq = torch.empty(H * d, device="cuda", dtype=dtype)
+    gg = torch.empty(H * d, device="cuda", dtype=dtype)
+    ref.split_q_gate(packed, H, d, qq, gg)
+    assert torch.equal(qq.view(H, d), packed.view(H, 2, d)[:, 0])
+    assert torch.equal(gg.view(H, d), packed.view(H, 2, d)[:, 1])
+    q_raw = qq.clone()
+    ref.head_rmsnorm(qq, qnw, H, d, eps, qq)
+    ref.rope_inplace(qq, H, d, S - 1, theta)
+    want = _ref(qq, kc, vc, H, Hkv, d, S, table, P)
+    ref.sigmoid_mul_inplace(want, gg, H * d)
+    w = q.Workspace(H, Hkv, d, S)
+    outs = []
+    for interleaved in (True, False):
+        out = torch.full((H * d,), float("nan"), device="cuda", dtype=dtype)
+        q.decode_attention(q=packed if interleaved else q_raw, gate=None if interleaved else gg, k_cache=kc,
+                           v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=S,
+                           page_table=table, page_size=P, q_norm_w=qnw, eps=eps, rope_theta=theta, fuse_q=True,
+                           workspace=w, deterministic=True, q_gate_interleaved=interleaved)
+        torch.cuda.synchronize()
+        assert w.status() == 0
+        outs.append(out)
+    ok, err, idx = allclose_report(outs[0], want, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+
+
+def test_interleaved_q_gate_rejects_a_second_gate():
+    H, Hkv, d, S = 8, 8, 128, 64
+    qv, kc, vc, _ = _inputs(H, Hkv, d, S, 16, torch.bfloat16, seed=63)
+    packed = torch.cat([qv.view(H, d), qv.view(H, d)], dim=1).flatten()
+    out = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="INVALID_VALUE"):
+        q.decode_attention(q=packed, gate=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv,
+                           head_dim=d, seq_len=S, q_gate_interleaved=True)

@@ -108,3 +108,30 @@ def test_pdl_chain_matches_plain_launches():
         outs.append((inp.out.clone(), inp.k_cache.clone()))
     assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
     assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+
+
+def test_batched_interleaved_q_gate_matches_split():
+    """Batched calls with the [B, H, 2d] interleaved q/gate projection give the same
+    bytes as calls on the split q [B, H, d] and gate [B, H, d]."""
+    cfg = _small_cfg(seed=13)
+    lens = [3, 900, 2100, 64]
+    H, d = cfg.num_heads, cfg.head_dim
+    outs = []
+    for interleaved in (True, False):
+        inp = make_batched_inputs(cfg, seq_lens=lens)
+        g = torch.Generator(device="cuda").manual_seed(14)
+        gate = torch.randn(len(lens), H, d, generator=g, device="cuda").to(inp["q"].dtype)
+        qraw = inp["q"].view(len(lens), H, d)
+        packed = torch.cat([qraw, gate], dim=2).contiguous()
+        plan = q.BatchPlan(lens, H, cfg.num_kv_heads, d)
+        q.batch_decode_attention(plan=plan, q=packed if interleaved else qraw, gate=None if interleaved else gate,
+                                 k_cache=inp["k_cache"], v_cache=inp["v_cache"], block_tables=inp["block_tables"],
+                                 out=inp["out"], num_heads=H, num_kv_heads=cfg.num_kv_heads, head_dim=d,
+                                 page_size=cfg.page_size, q_norm_w=inp["q_norm_w"], k_norm_w=inp["k_norm_w"],
+                                 k_new=inp["k_new"], v_new=inp["v_new"], fuse_q=True, fuse_append=True,
+                                 q_gate_interleaved=interleaved)
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+        outs.append((inp["out"].clone(), inp["k_cache"].clone()))
+    assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
+    assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))

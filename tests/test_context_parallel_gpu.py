@@ -235,13 +235,19 @@ def _gated_case(S, seed, dtype=torch.bfloat16):
     return (Hg, Hkvg, Dg), kw
 
 
-def test_fused_exchange_world1_gated_d256():
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_fused_exchange_world1_gated_d256(interleaved):
     """Gated d=256 shape through the fused exchange at world 1: bit-identical to the
-    plain call (gate applied once, after the merge), two calls in a row. Both run with
-    QIC_DETERMINISTIC: at this length the stage pool would otherwise change the order
-    of the split sums from call to call."""
+    plain call (gate applied once, after the merge), two calls in a row; with
+    `interleaved` the exchange call reads q and the gate from the packed [H, 2d]
+    projection. Both run with QIC_DETERMINISTIC: at this length the stage pool would
+    otherwise change the order of the split sums from call to call."""
     S = 16385
     (Hg, Hkvg, Dg), kw = _gated_case(S, seed=41)
+    kw_cp = dict(kw)
+    if interleaved:
+        packed = torch.cat([kw["q"].view(Hg, Dg), kw["gate"].view(Hg, Dg)], dim=1).flatten()
+        kw_cp.update(q=packed, gate=None, q_gate_interleaved=True)
     group = cpm.ExchangeGroup(Hg, Hkvg, Dg, rank=0, world=1, gather=lambda b, r, n: [b])
     try:
         ws_cp = q.Workspace(Hg, Hkvg, Dg, S)
@@ -250,7 +256,7 @@ def test_fused_exchange_world1_gated_d256():
             out_cp = torch.full((Hg * Dg,), float("nan"), device="cuda", dtype=torch.bfloat16)
             out = torch.empty(Hg * Dg, device="cuda", dtype=torch.bfloat16)
             cpm.cp_decode_attention(group, out=out_cp, workspace=ws_cp, position=S - 1, cluster_size=8,
-                                    deterministic=True, **kw)
+                                    deterministic=True, **kw_cp)
             q.decode_attention(out=out, workspace=ws, cluster_size=8, deterministic=True, **kw)
             torch.cuda.synchronize()
             assert ws_cp.status() == 0 and ws.status() == 0
