@@ -20,20 +20,24 @@ batch partitioned by K/V bytes (strong scaling: total bytes / the slowest rank's
 time). --workload qwen3_8b_s131073 or qwen3_8b_batch64 with N > 1 makes those the
 line's value.
 
-Other workloads (--workload): qwen3_0p6b_s1025 (one layer), qwen35_gated_s32769 (d=256
-with the output gate; 8 layers chained like the full-attention layers of a hybrid
-stack, each with its own 32K cache), qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step;
-state bytes), qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64
-(64 sequences, lengths 512..32768, one shared page pool, one batched launch).
+Other workloads (--workload): qwen3_0p6b_s1025 (one layer), qwen35_gated_s32769 (d=256;
+q is the interleaved q/gate projection and the output is gated; 8 layers chained like
+the full-attention layers of a hybrid stack, each with its own 32K cache),
+qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step; state bytes),
+qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64 (64 sequences,
+lengths 512..32768, one shared page pool, one batched launch).
 
---impl reference (rank 0 only): the reference's attention on the host cores — the
-oracle's C restatement of src/kernels.cu's paged attention, OpenMP over heads — as the
-line's value, plus the reference's own kernels built for sm_100a timed on the GPU.
+--impl reference (rank 0 only): the reference's implementation of the same workload
+on the host cores, as the line's value: the oracle's C restatement of src/kernels.cu's
+paged attention and of the GatedDeltaNet host loop (src/model.cpp:692-793), OpenMP
+over heads, on a bounded sample. For the attention workloads the reference's own
+kernels built for sm_100a are also timed on the GPU.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
+import dataclasses
 import json
 import os
 import statistics
@@ -515,34 +519,98 @@ def measure(wl, args, world, local):
 # ---------------------------------------------------------------------------
 # CPU baseline and the reference arm
 # ---------------------------------------------------------------------------
-def cpu_baseline(cfg, budget_s=6.0):
-    """The oracle (C restatement of the reference's paged attention, OpenMP over
-    heads) on a bounded sample of the workload's layers on this host."""
+def _timed_loop(fn, budget_s):
+    """Runs fn until budget_s seconds have passed; returns (calls, seconds)."""
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            return n, el
+
+
+def cpu_baseline(workload, budget_s=6.0):
+    """The oracle (C restatement of the reference's path, OpenMP over heads) on a
+    bounded sample of `workload` on this host's cores, in the workload's metric.
+    Attention: whole layers at the workload's S. GatedDeltaNet: whole steps (the
+    reference runs this block as a host loop, src/model.cpp:692-793). Pair: both.
+    Batch: whole steps over the first sequences of the seeded length list."""
     from oracle.oracle import Oracle
-    from qwenincuda_b200.workloads import make_attention_inputs
+    from qwenincuda_b200.workloads import (CONFIGS, BatchConfig, GdnConfig, batched_bytes, make_attention_inputs,
+                                           make_batched_inputs, make_gdn_inputs)
 
     orc = Oracle()
     # every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1)
     orc.set_num_threads(len(os.sched_getaffinity(0)))
     threads = orc.num_threads()
-    inp = make_attention_inputs(cfg, paged=True, layers=1, device="cpu")
-    H, Hkv, d, S = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len
-    kc = inp.k_cache[0].view(-1, Hkv * d)
-    vc = inp.v_cache[0].view(-1, Hkv * d)
-    layers = 0
-    t0 = time.perf_counter()
-    while True:
-        orc.attention(inp.q[0].flatten(), kc, vc, H, Hkv, d, S, page_table=inp.page_table[0],
-                      page_size=cfg.page_size)
-        layers += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s:
-            break
-    per_layer = el / layers
-    lb = cfg.kv_read_bytes() + cfg.append_bytes()
-    return {"value": round(lb / per_layer / 1e9, 3), "unit": "GB/s", "us_per_layer": round(per_layer * 1e6, 1),
-            "cores": threads, "kind": "port",
-            "sample": f"{layers} layers of paged attention at S={S} (H={H}, Hkv={Hkv}, d={d}) in {el:.1f} s"}
+
+    def attention_layer(cfg):
+        inp = make_attention_inputs(cfg, paged=True, layers=1, device="cpu")
+        H, Hkv, d, S = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.seq_len
+        kc = inp.k_cache[0].view(-1, Hkv * d)
+        vc = inp.v_cache[0].view(-1, Hkv * d)
+        gate = inp.gate[0].flatten() if inp.gate is not None else None
+
+        def run():
+            o = orc.attention(inp.q[0].flatten(), kc, vc, H, Hkv, d, S, page_table=inp.page_table[0],
+                              page_size=cfg.page_size)
+            if gate is not None:
+                orc.sigmoid_mul(o, gate)
+
+        return run, cfg.kv_read_bytes() + cfg.append_bytes(), f"paged attention at S={S} (H={H}, Hkv={Hkv}, d={d})"
+
+    def gdn_step():
+        cfg = GdnConfig()
+        t = make_gdn_inputs(cfg, device="cpu")
+        kw = {k: t[k] for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state",
+                                "recurrent_state")}
+
+        def run():
+            orc.gated_delta(num_k_heads=cfg.num_k_heads, num_v_heads=cfg.num_v_heads, conv_kernel=cfg.conv_kernel,
+                            eps=cfg.eps, **kw)
+
+        return run, cfg.state_bytes(), f"GatedDeltaNet decode (Hk={cfg.num_k_heads}, Hv={cfg.num_v_heads}, d=128)"
+
+    if workload in ATTN_WORKLOADS:
+        run, nbytes, what = attention_layer(CONFIGS[workload])
+        unit_name = "layers"
+    elif workload == "qwen35_gdn":
+        run, nbytes, what = gdn_step()
+        unit_name = "steps"
+    elif workload == "qwen35_pair":
+        g_run, g_bytes, _ = gdn_step()
+        a_run, a_bytes, a_what = attention_layer(CONFIGS["qwen35_gated_s32769"])
+
+        def run():
+            g_run()
+            a_run()
+
+        nbytes, what, unit_name = g_bytes + a_bytes, f"GatedDeltaNet step + gated {a_what}", "steps"
+    elif workload == "qwen3_8b_batch64":
+        cfg = BatchConfig()
+        lens = cfg.seq_lens()[:4]
+        # a pool just large enough for the sample (the full pool is 4.5 GB)
+        cfg = dataclasses.replace(cfg, pool_tokens=sum(lens) + len(lens) * cfg.page_size)
+        inp = make_batched_inputs(cfg, device="cpu", seq_lens=lens)
+        qs = inp["q"].view(len(lens), -1)
+        kc = inp["k_cache"].view(-1, cfg.kv_dim)
+        vc = inp["v_cache"].view(-1, cfg.kv_dim)
+        sl = torch.tensor(lens, dtype=torch.int32)
+
+        def run():
+            orc.batched_attention(qs, kc, vc, inp["block_tables"], sl, cfg.page_size, cfg.num_heads,
+                                  cfg.num_kv_heads, cfg.head_dim)
+
+        nbytes = batched_bytes(lens, cfg.kv_dim)
+        what, unit_name = f"batched paged attention over the first {len(lens)} of the 64 sequences ({sum(lens)} tokens)", "steps"
+    else:
+        raise SystemExit(f"unknown workload {workload}")
+    n, el = _timed_loop(run, budget_s)
+    per = el / n
+    return {"value": round(nbytes / per / 1e9, 3), "unit": "GB/s", f"us_per_{unit_name[:-1]}": round(per * 1e6, 1),
+            "cores": threads, "kind": "port", "sample": f"{n} {unit_name} of {what} in {el:.1f} s"}
 
 
 def reference_gpu(cfg, layers, steps, warmup):
@@ -602,28 +670,56 @@ def reference_gpu(cfg, layers, steps, warmup):
 
 
 def run_reference_arm(args, world, rank):
-    from qwenincuda_b200.workloads import CONFIGS
+    """The reference's own implementation of the path on this host's cores, on the
+    same workload, metric and unit as this library's line (rank 0 only). For the
+    attention workloads the reference's kernels built for sm_100a are also timed on
+    the GPU, as extra information."""
+    from qwenincuda_b200.workloads import CONFIGS, BatchConfig, GdnConfig, batched_bytes
 
     if rank != 0:
         return
-    name = args.workload if args.workload in ATTN_WORKLOADS else "qwen3_8b_s8192"
-    cfg = CONFIGS[name]
-    cb = cpu_baseline(cfg, budget_s=max(2.0, min(20.0, 0.5 * args.steps)))
+    name = args.workload
+    cb = cpu_baseline(name, budget_s=max(2.0, min(20.0, 0.5 * args.steps)))
+    layers = 1
+    if name in ATTN_WORKLOADS:
+        cfg = CONFIGS[name]
+        layers = cfg.layers
+        config = {"layout": "paged", "layers": layers, "seq_len": cfg.seq_len, "num_heads": cfg.num_heads,
+                  "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim, "gate": cfg.gate}
+        step_bytes = (cfg.kv_read_bytes() + cfg.append_bytes()) * layers
+    elif name == "qwen35_gdn":
+        g = GdnConfig()
+        config = {"num_k_heads": g.num_k_heads, "num_v_heads": g.num_v_heads, "k_head_dim": g.k_head_dim,
+                  "v_head_dim": g.v_head_dim, "conv_dim": g.conv_dim, "conv_kernel": g.conv_kernel}
+        step_bytes = g.state_bytes()
+    elif name == "qwen35_pair":
+        att = CONFIGS["qwen35_gated_s32769"]
+        config = {"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)"}
+        step_bytes = GdnConfig().state_bytes() + att.kv_read_bytes() + att.append_bytes()
+    else:
+        b = BatchConfig()
+        config = {"batch": b.batch, "seq_lens": f"U[{b.min_len},{b.max_len}]+1, seed {b.seed}",
+                  "page_size": b.page_size, "num_heads": b.num_heads, "num_kv_heads": b.num_kv_heads,
+                  "head_dim": b.head_dim}
+        step_bytes = batched_bytes(b.seq_lens(), b.kv_dim)
+    # the whole step of the workload at the sample's rate
+    ms_step = step_bytes / (cb["value"] * 1e9) * 1e3
     line = {
-        "impl": "reference", "metric": "decode-attn KV-read GB/s", "value": cb["value"], "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(cb["us_per_layer"] * cfg.layers / 1000, 3), "us_per_layer": cb["us_per_layer"],
+        "impl": "reference",
+        "metric": "GatedDeltaNet state GB/s" if name == "qwen35_gdn" else "decode-attn KV-read GB/s",
+        "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 3), "us_per_layer": round(ms_step * 1000 / layers, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": name, "layout": "paged", "layers": cfg.layers, "seq_len": cfg.seq_len,
-                   "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim},
+        "config": {"workload": name, "parallelism": "single", **config},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    try:
-        line["reference_kernels_sm100a"] = reference_gpu(cfg, layers=min(2, cfg.layers),
-                                                         steps=max(1, min(5, args.steps // 20)), warmup=1)
-    except Exception as exc:  # extra information only
-        line["reference_kernels_sm100a"] = {"unavailable": str(exc)[:200]}
+    if name in ATTN_WORKLOADS:
+        try:
+            line["reference_kernels_sm100a"] = reference_gpu(CONFIGS[name], layers=min(2, layers),
+                                                             steps=max(1, min(5, args.steps // 20)), warmup=1)
+        except Exception as exc:  # extra information only
+            line["reference_kernels_sm100a"] = {"unavailable": str(exc)[:200]}
     print(json.dumps(line), flush=True)
 
 
@@ -726,10 +822,8 @@ def main():
         "gpu_launches": wl["launches"] * args.steps,
         "clocks": clocks,
     }
-    if world == 1 and rank == 0 and not args.no_cpu_baseline and args.workload in ATTN_WORKLOADS:
-        from qwenincuda_b200.workloads import CONFIGS
-
-        line["cpu_baseline"] = cpu_baseline(CONFIGS[args.workload])
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
