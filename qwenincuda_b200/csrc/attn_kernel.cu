@@ -699,8 +699,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
     }
   }
-  // every CTA of the cluster has read the partials it needs from this one
-  cluster_sync_all();
+  // This CTA's reads of its peers' partials are complete (their values are consumed
+  // above), so it tells the cluster with a relaxed arrive. The matching wait is the
+  // last thing before exit (shared memory must outlive the peers' reads), so the
+  // cross-cluster step below does not wait for the rest of the cluster.
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   if (nclust > 1) {
     // ---- merge the cluster partials of this slice: last arriving cluster ----
     consumer_sync();
@@ -820,6 +823,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
   }
+  asm volatile("barrier.cluster.wait;" ::: "memory");
 }
 
 // ----------------------------------------------------------------------------
