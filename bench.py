@@ -23,7 +23,8 @@ line's value.
 Other workloads (--workload): qwen3_0p6b_s1025 (one layer), qwen35_gated_s32769 (d=256;
 q is the interleaved q/gate projection and the output is gated; 8 layers chained like
 the full-attention layers of a hybrid stack, each with its own 32K cache),
-qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (GatedDeltaNet step; state bytes),
+qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (32 chained GatedDeltaNet layers,
+each with its own state; state bytes),
 qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64 (64 sequences,
 lengths 512..32768, one shared page pool, one batched launch).
 
@@ -53,6 +54,7 @@ sys.path.insert(0, str(ROOT))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 ATTN_WORKLOADS = ("qwen3_0p6b_s1025", "qwen3_8b_s8192", "qwen35_gated_s32769", "qwen3_8b_s131073")
+GDN_STACK_LAYERS = 32  # GatedDeltaNet layers per qwen35_gdn step: 146 MB, more than L2
 
 
 def load_peaks():
@@ -276,40 +278,60 @@ def _pack(tensors):
     return buf, views
 
 
-def gdn_workload():
+def gdn_workload(layers=GDN_STACK_LAYERS):
+    """`layers` GatedDeltaNet layers of a hybrid stack, each with its own state and
+    weights, chained with programmatic dependent launch: 32 layers move 146 MB of
+    state and inputs per step, more than L2 holds."""
+    import dataclasses
+
     import qwenincuda_b200 as q
     from qwenincuda_b200.workloads import GdnConfig, make_gdn_inputs
 
     cfg = GdnConfig()
-    t = make_gdn_inputs(cfg)
-    packed, views = _pack([t["qkv"], t["z"], t["b"], t["a"]])  # one host-to-device copy per step
-    t["qkv"], t["z"], t["b"], t["a"] = views
-    g = q.GdnArgs()
-    g.dtype = 1
-    g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
-    g.conv_kernel, g.eps = cfg.conv_kernel, cfg.eps
-    g.flags = q.abi.QIC_PDL  # the layer after it may start its copies while it runs
-    for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state", "out"):
-        setattr(g, k, t[k].data_ptr())
-    step = _call(q.lib().qic_gated_delta_decode, g)
+    stack = [make_gdn_inputs(dataclasses.replace(cfg, seed=cfg.seed + 1000 * l)) for l in range(layers)]
+    # every layer's step inputs in one buffer (one host-to-device copy per step), every
+    # layer's output in another (one device-to-host copy)
+    packed, views = _pack([t[k] for t in stack for k in ("qkv", "z", "b", "a")])
+    outs, out_views = _pack([t["out"] for t in stack])
+    for i, t in enumerate(stack):
+        t["qkv"], t["z"], t["b"], t["a"] = views[4 * i:4 * i + 4]
+        t["out"] = out_views[i]
+    fns, args = [], []
+    for t in stack:
+        g = q.GdnArgs()
+        g.dtype = 1
+        g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
+        g.conv_kernel, g.eps = cfg.conv_kernel, cfg.eps
+        g.flags = q.abi.QIC_PDL  # the next layer may start its weight loads and prefetches while this one runs
+        for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state",
+                  "out"):
+            setattr(g, k, t[k].data_ptr())
+        args.append(g)
+        fns.append(_call(q.lib().qic_gated_delta_decode, g))
+
+    def step():
+        for f in fns:
+            f()
+
     hin = packed.cpu().pin_memory()
-    hout = torch.empty_like(t["out"], device="cpu").pin_memory()
+    hout = torch.empty_like(outs, device="cpu").pin_memory()
 
     def e2e():
         packed.copy_(hin, non_blocking=True)
         step()
-        hout.copy_(t["out"], non_blocking=True)
+        hout.copy_(outs, non_blocking=True)
 
     h2d = hin.numel() * hin.element_size()
-    return dict(step=step, bytes=cfg.state_bytes(), launches=1, bytes_per_launch=cfg.state_bytes(),
-                e2e=(e2e, h2d, hout.numel() * 2), kernel="gated_delta_kernel", status=lambda: 0, keep=(t, g, packed),
-                config={"num_k_heads": cfg.num_k_heads, "num_v_heads": cfg.num_v_heads, "k_head_dim": 128,
-                        "v_head_dim": 128, "conv_dim": cfg.conv_dim, "conv_kernel": cfg.conv_kernel,
-                        "state": "fp32, resident on the device"})
+    return dict(step=step, bytes=cfg.state_bytes() * layers, launches=layers, bytes_per_launch=cfg.state_bytes(),
+                e2e=(e2e, h2d, hout.numel() * hout.element_size()), kernel="gated_delta_kernel", status=lambda: 0,
+                keep=(stack, args, packed, outs),
+                config={"layers": layers, "num_k_heads": cfg.num_k_heads, "num_v_heads": cfg.num_v_heads,
+                        "k_head_dim": 128, "v_head_dim": 128, "conv_dim": cfg.conv_dim,
+                        "conv_kernel": cfg.conv_kernel, "state": "fp32, resident on the device, one per layer"})
 
 
 def pair_workload():
-    gdn = gdn_workload()
+    gdn = gdn_workload(layers=1)
     att = attention_workload("qwen35_gated_s32769", "paged", layers=1)
 
     def step():
@@ -689,9 +711,11 @@ def run_reference_arm(args, world, rank):
         step_bytes = (cfg.kv_read_bytes() + cfg.append_bytes()) * layers
     elif name == "qwen35_gdn":
         g = GdnConfig()
-        config = {"num_k_heads": g.num_k_heads, "num_v_heads": g.num_v_heads, "k_head_dim": g.k_head_dim,
-                  "v_head_dim": g.v_head_dim, "conv_dim": g.conv_dim, "conv_kernel": g.conv_kernel}
-        step_bytes = g.state_bytes()
+        layers = GDN_STACK_LAYERS
+        config = {"layers": layers, "num_k_heads": g.num_k_heads, "num_v_heads": g.num_v_heads,
+                  "k_head_dim": g.k_head_dim, "v_head_dim": g.v_head_dim, "conv_dim": g.conv_dim,
+                  "conv_kernel": g.conv_kernel}
+        step_bytes = g.state_bytes() * layers
     elif name == "qwen35_pair":
         att = CONFIGS["qwen35_gated_s32769"]
         config = {"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)"}

@@ -311,8 +311,10 @@ typedef struct qic_gdn_args {
   int32_t v_head_dim;       /* dv == 128 */
   int32_t conv_kernel;      /* K in [1, 8] */
   float eps;                /* gated RMSNorm epsilon */
-  uint32_t flags;           /* QIC_PDL: may start while the previous kernel in the stream runs;
-                               every input and the state are read after it has completed. The
+  uint32_t flags;           /* QIC_PDL: may start while the previous kernel in the stream runs,
+                               loading the weights (conv_w, dt_bias, a_log, norm_w, which no kernel
+                               may write meanwhile) and prefetching the states into L2; the states
+                               and qkv, z, b, a are read after that kernel has completed. The
                                kernel always lets the next kernel in the stream start early. */
   const void* qkv;          /* [2*Hk*dk + Hv*dv] in_proj_qkv output (conv input) */
   const void* z;            /* [Hv*dv] */

@@ -35,7 +35,7 @@ constexpr int kGdnDk = 128;
 constexpr int kGdnDv = 128;
 
 template <typename T, int REP, int CB>
-__global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_args a) {
+__global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_gdn_args a) {
   constexpr int NC = kGdnDv / CB;            // state columns owned by this CTA
   constexpr int QUADS = NC / 4;              // float4 column groups
   constexpr int RG = kGdnThreads / QUADS;    // row groups
@@ -43,10 +43,8 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   static_assert(RPT * RG == kGdnDk, "row split");
 
   // the next kernel in the stream may start (its own griddepcontrol.wait keeps it
-  // from reading this kernel's outputs early); this kernel reads its inputs and the
-  // state only after the kernel before it has completed
+  // from reading this kernel's outputs early)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int vloc = rank / CB;
@@ -69,29 +67,57 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
   const T* conv_w = static_cast<const T*>(a.conv_w);
   float* conv_state = a.conv_state;
 
-  // ---- 0. every global load that does not depend on another is issued first, so
-  // the state block, the gate scalars and the output-gate inputs arrive together
-  // with the conv inputs instead of in sequence ----
+  // ---- 0. every global load that does not depend on another is issued first. The
+  // weights (conv taps, dt_bias, a_log, norm_w) are never written by a kernel, so they
+  // are loaded before griddepcontrol.wait, while the preceding kernel may still run.
+  // The states may be written by an earlier kernel that is still running (with
+  // programmatic dependent launch a kernel further back in the stream can be, e.g.
+  // this layer's previous step): before the wait they are only prefetched into L2,
+  // the point of coherence, and read after it together with the step's inputs ----
   const int quad = tid % QUADS;
   const int rg = tid / QUADS;
   float* state = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv + cb * NC + quad * 4;
+  // thread t: q channel t and k channel t of key head kh; v channel t (t < NC)
+  const int cq = kh * kGdnDk + tid;
+  const int ck = Hk * kGdnDk + kh * kGdnDk + tid;
+  const int cv = 2 * Hk * kGdnDk + vh * kGdnDv + cb * NC + tid;
+  // row `tid` of this CTA's state block (NC columns: one or two lines) and the three
+  // conv windows
+  {
+    const float* row = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv +
+                       static_cast<size_t>(tid) * kGdnDv + cb * NC;
+#pragma unroll
+    for (int c = 0; c < NC; c += 32) prefetch_l2(row + c);
+  }
+  prefetch_l2(conv_state + static_cast<size_t>(cq) * K);
+  prefetch_l2(conv_state + static_cast<size_t>(ck) * K);
+  if (tid < NC) prefetch_l2(conv_state + static_cast<size_t>(cv) * K);
+  const T dt_raw = static_cast<const T*>(a.dt_bias)[vh];
+  const T al_raw = static_cast<const T*>(a.a_log)[vh];
+  T nw_raw = T();
+  if (tid < NC) nw_raw = static_cast<const T*>(a.norm_w)[cb * NC + tid];
+  T wt_q[8], wt_k[8], wt_v[8];  // conv taps of the three channels
+  auto taps = [&](int c, T (&wt)[8]) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) wt[t] = (t < K) ? conv_w[static_cast<size_t>(c) * K + t] : T();
+  };
+  taps(cq, wt_q);
+  taps(ck, wt_k);
+  if (tid < NC) taps(cv, wt_v);
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float4 s[RPT];
 #pragma unroll
   for (int r = 0; r < RPT; ++r) s[r] = *reinterpret_cast<const float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv);
   const T bv_raw = static_cast<const T*>(a.b)[vh];
   const T av_raw = static_cast<const T*>(a.a)[vh];
-  const T dt_raw = static_cast<const T*>(a.dt_bias)[vh];
-  const T al_raw = static_cast<const T*>(a.a_log)[vh];
-  T z_raw = T(), nw_raw = T();
-  if (tid < NC) {
-    z_raw = static_cast<const T*>(a.z)[static_cast<size_t>(vh) * kGdnDv + cb * NC + tid];
-    nw_raw = static_cast<const T*>(a.norm_w)[cb * NC + tid];
-  }
+  T z_raw = T();
+  if (tid < NC) z_raw = static_cast<const T*>(a.z)[static_cast<size_t>(vh) * kGdnDv + cb * NC + tid];
 
   // ---- 1. causal conv + SiLU from the old conv state ----
-  // thread t: q channel t and k channel t of key head kh; v channel t (t < NC)
+  // win: the channel's new window [old[1..K-1], x]
   float win_q[8], win_k[8], win_v[8];
-  auto conv_channel = [&](int c, float (&win)[8]) -> float {
+  auto conv_channel = [&](int c, float (&win)[8], const T (&wt)[8]) -> float {
     const float x = to_f32<T>(qkv[c]);
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
@@ -100,16 +126,13 @@ __global__ void __launch_bounds__(kGdnThreads) gated_delta_kernel(const qic_gdn_
     float acc = 0.0f;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      if (t < K) acc = __fadd_rn(acc, __fmul_rn(to_f32<T>(conv_w[static_cast<size_t>(c) * K + t]), win[t]));
+      if (t < K) acc = __fadd_rn(acc, __fmul_rn(to_f32<T>(wt[t]), win[t]));
     }
     return acc / (1.0f + expf(-acc));
   };
-  const int cq = kh * kGdnDk + tid;
-  const int ck = Hk * kGdnDk + kh * kGdnDk + tid;
-  const int cv = 2 * Hk * kGdnDk + vh * kGdnDv + cb * NC + tid;
-  q_s[tid] = conv_channel(cq, win_q);
-  k_s[tid] = conv_channel(ck, win_k);
-  if (tid < NC) v_s[tid] = conv_channel(cv, win_v);
+  q_s[tid] = conv_channel(cq, win_q, wt_q);
+  k_s[tid] = conv_channel(ck, win_k, wt_k);
+  if (tid < NC) v_s[tid] = conv_channel(cv, win_v, wt_v);
 
   // every CTA of the cluster has read the old conv state past this point (first
   // phase of the cluster barrier; the conv-state writes wait for it further down)

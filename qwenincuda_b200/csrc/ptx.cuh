@@ -70,6 +70,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 // ----------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
 // ----------------------------------------------------------------------------
+// Brings the 128-byte line holding `p` into L2 (no value is read).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
