@@ -62,8 +62,12 @@ enum {
   QIC_PDL = 4,                   /* programmatic dependent launch: the kernel may start while the previous
                                     kernel in the stream runs and prefetch cached K/V rows (all but the
                                     appended one) and page-table entries; q, k_new, v_new, gate and the
-                                    workspace are touched only after that kernel has completed. The
-                                    previous kernel must not write the page table or those cached rows. */
+                                    workspace are touched only after that kernel has completed. No
+                                    kernel that can still be running may write the page table or those
+                                    cached rows: when every kernel in between lets its dependents start
+                                    early (this one does), that includes kernels several launches back.
+                                    In a layer stack their writers (this layer's previous step, the
+                                    caller's page-table update) are a whole stack of layers back. */
   QIC_PARTIAL_OUT = 8,           /* out is float [Hkv][qic_partial_floats()]: per kv head, the G*d
                                     outputs normalised by their own softmax sum, then G log-sum-exp
                                     values (log2 of the sum of 2^(score*log2(e)/sqrt(d))), padded to a
