@@ -334,12 +334,26 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
     // resident slots is left free, so the next launch's CTAs start their copies while
     // this one merges its splits (measured on 36 chained S=8192 layers: 13.6 -> 12.8
     // us per layer; 8 chained d=256 S=32769 layers: 31.3 -> 30.2 us).
+    const bool auto_cluster = cluster == 0;
     if (cluster == 0) cluster = 8;
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
     int nclust = std::max(1, max_clusters / Hkv);
     n_splits = cluster * nclust;
+    if (auto_cluster) {
+      // Shorter sequences: about 6 stages per CTA (8 at d=256; 12 at d=64, the same
+      // bytes as d=128, not swept), in multiples of 8 CTAs, and a single cluster per
+      // kv head up to 16 CTAs, so the merge needs no cross-cluster step. Measured on
+      // 8 chained layers: d=128 S=1025 10.0 -> 8.9 us, S=2049 10.5 -> 9.5, S=4097
+      // 12.0 -> 11.5; d=256 S=2049 14.0 -> 12.1, S=8193 16.7 -> 15.6.
+      const int per_split = D >= 256 ? 8 : (D >= 128 ? 6 : 12);
+      const int want = std::max(8, n_stages / per_split / 8 * 8);
+      if (want < n_splits) {
+        n_splits = want;
+        if (want <= qic::kMaxCluster) cluster = want;
+      }
+    }
     if (n_splits > n_stages) {
       nclust = std::max(1, n_stages / cluster);
       if (n_stages < cluster) cluster = n_stages;
