@@ -20,7 +20,8 @@ batch partitioned by K/V bytes (strong scaling: total bytes / the slowest rank's
 time). --workload qwen3_8b_s131073 or qwen3_8b_batch64 with N > 1 makes those the
 line's value.
 
-Other workloads (--workload): qwen3_0p6b_s1025 (one layer), qwen35_gated_s32769 (d=256;
+Other workloads (--workload): qwen3_0p6b_s1025 (32 chained layers of S=1025, each with
+its own cache: 134 MB per step), qwen35_gated_s32769 (d=256;
 q is the interleaved q/gate projection and the output is gated; 8 layers chained like
 the full-attention layers of a hybrid stack, each with its own 32K cache),
 qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (32 chained GatedDeltaNet layers,
@@ -394,14 +395,15 @@ def batched_workload(world, rank):
                         "head_dim": cfg.head_dim})
 
 
-def cp_workload(world, rank, with_allgather=True):
+def cp_workload(world, rank, with_allgather=True, layers=2):
     """One 131073-token sequence (Qwen3-8B attention shape, page 16, shuffled tables)
-    split into N contiguous page ranges, one per rank (shard_tokens). A step is one
-    fused qic_cp_decode_attention per rank: q prologue at the global position, the
-    append on the rank that holds the last token, attention over the rank's shard,
-    and the in-kernel NVLink exchange + log-sum-exp merge of the ranks' partials.
-    Each rank's shard is seeded independently; q, k_new and v_new are the same on
-    every rank."""
+    in each of `layers` layers, split into N contiguous page ranges, one per rank
+    (shard_tokens). A step is one fused qic_cp_decode_attention per rank and layer: q
+    prologue at the global position, the append on the rank that holds the last token,
+    attention over the rank's shard, and the in-kernel NVLink exchange + log-sum-exp
+    merge of the ranks' partials. Two layers keep a rank's K/V per step (134 MB at 8
+    ranks) larger than L2. Each rank's shards are seeded independently; q, k_new and
+    v_new are the same on every rank."""
     import qwenincuda_b200 as q
     from qwenincuda_b200 import context_parallel as cpm
     from qwenincuda_b200.workloads import CONFIGS
@@ -413,40 +415,44 @@ def cp_workload(world, rank, with_allgather=True):
     pages = (n + P - 1) // P
     dtype = torch.bfloat16
     g = torch.Generator(device="cuda").manual_seed(cfg.seed * 1000 + 17 * rank + 1)
-    kc = (torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype)
-    vc = (torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype)
-    table = torch.randperm(pages, generator=g, device="cuda").to(torch.int32)
+    kcs = [(torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype) for _ in range(layers)]
+    vcs = [(torch.randn(pages * P, Hkv * d, generator=g, device="cuda") * cfg.kv_std).to(dtype) for _ in range(layers)]
+    tables = [torch.randperm(pages, generator=g, device="cuda").to(torch.int32) for _ in range(layers)]
     gs = torch.Generator(device="cuda").manual_seed(cfg.seed * 1000 + 999)
-    qv = torch.randn(H * d, generator=gs, device="cuda").to(dtype)
-    kn = torch.randn(Hkv * d, generator=gs, device="cuda").to(dtype)
-    vn = (torch.randn(Hkv * d, generator=gs, device="cuda") * cfg.kv_std).to(dtype)
-    packed, (qv, kn, vn) = _pack([qv, kn, vn])  # one host-to-device copy per step
+    ins = []
+    for _ in range(layers):
+        ins += [torch.randn(H * d, generator=gs, device="cuda").to(dtype),
+                torch.randn(Hkv * d, generator=gs, device="cuda").to(dtype),
+                (torch.randn(Hkv * d, generator=gs, device="cuda") * cfg.kv_std).to(dtype)]
+    packed, ins = _pack(ins)  # one host-to-device copy per step
     ones = torch.ones(d, device="cuda", dtype=dtype)
-    out = torch.zeros(H * d, device="cuda", dtype=dtype)
-    ws = q.Workspace(H, Hkv, d, n)
+    outs, out_views = _pack([torch.zeros(H * d, device="cuda", dtype=dtype) for _ in range(layers)])
+    ws = q.Workspace(H, Hkv, d, n)  # the layers' calls are in stream order: one workspace, one exchange group
     owner = rank == world - 1
     group = cpm.ExchangeGroup(H, Hkv, d, rank, world)
-    kw = dict(q=qv, k_cache=kc, v_cache=vc, num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=n, page_table=table,
-              page_size=P, q_norm_w=ones, k_norm_w=ones, k_new=kn, v_new=vn, eps=cfg.eps, rope_theta=cfg.rope_theta,
-              fuse_q=True, fuse_append=owner, workspace=ws, cache_tokens=pages * P, position=S - 1)
-    a = q.ops.decode_args(out=out, **kw)
+    kws = [dict(q=ins[3 * l], k_cache=kcs[l], v_cache=vcs[l], num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=n,
+                page_table=tables[l], page_size=P, q_norm_w=ones, k_norm_w=ones, k_new=ins[3 * l + 1],
+                v_new=ins[3 * l + 2], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True, fuse_append=owner,
+                workspace=ws, cache_tokens=pages * P, position=S - 1) for l in range(layers)]
+    args = [q.ops.decode_args(out=out_views[l], **kws[l]) for l in range(layers)]
     lib = q.lib()
     cp_ptr = ctypes.byref(group.args)
 
     def step():
-        rc = lib.qic_cp_decode_attention(ctypes.byref(a), cp_ptr, torch.cuda.current_stream().cuda_stream)
-        if rc != 0:
-            raise q.QicError(rc, "qic_cp_decode_attention")
+        for a in args:
+            rc = lib.qic_cp_decode_attention(ctypes.byref(a), cp_ptr, torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise q.QicError(rc, "qic_cp_decode_attention")
 
     hin = packed.cpu().pin_memory()
-    ho = torch.empty_like(out, device="cpu").pin_memory()
+    ho = torch.empty_like(outs, device="cpu").pin_memory()
 
     def e2e():
         packed.copy_(hin, non_blocking=True)
         step()
-        ho.copy_(out, non_blocking=True)
+        ho.copy_(outs, non_blocking=True)
 
-    nbytes = 2 * n * Hkv * d * 2 + (2 * Hkv * d * 2 if owner else 0)
+    per_layer = 2 * n * Hkv * d * 2 + (2 * Hkv * d * 2 if owner else 0)
     allgather = None
     if with_allgather and world > 1:
         import torch.distributed as dist
@@ -454,25 +460,26 @@ def cp_workload(world, rank, with_allgather=True):
         pf = q.ops.partial_floats(H, Hkv, d)
         part = torch.empty(Hkv * pf, device="cuda", dtype=torch.float32)
         gathered = torch.empty(world * Hkv * pf, device="cuda", dtype=torch.float32)
-        out2 = torch.zeros_like(out)
+        outs2 = [torch.zeros(H * d, device="cuda", dtype=dtype) for _ in range(layers)]
         ws2 = q.Workspace(H, Hkv, d, n)
-        kw2 = dict(kw, workspace=ws2, fuse_append=False)
-        a2 = q.ops.decode_args(out=part, partial_out=True, **kw2)
+        args2 = [q.ops.decode_args(out=part, partial_out=True, **dict(kws[l], workspace=ws2, fuse_append=False))
+                 for l in range(layers)]
 
         def ag_step():
-            rc = lib.qic_decode_attention(ctypes.byref(a2), torch.cuda.current_stream().cuda_stream)
-            if rc != 0:
-                raise q.QicError(rc, "qic_decode_attention")
-            dist.all_gather_into_tensor(gathered, part)
-            q.ops.attention_merge(gathered, H, Hkv, d, out2)
+            for l in range(layers):
+                rc = lib.qic_decode_attention(ctypes.byref(args2[l]), torch.cuda.current_stream().cuda_stream)
+                if rc != 0:
+                    raise q.QicError(rc, "qic_decode_attention")
+                dist.all_gather_into_tensor(gathered, part)
+                q.ops.attention_merge(gathered, H, Hkv, d, outs2[l])
 
         allgather = ag_step
-    return dict(step=step, bytes=nbytes, launches=1, bytes_per_launch=nbytes, partitioned=True,
+    return dict(step=step, bytes=per_layer * layers, launches=layers, bytes_per_launch=per_layer, partitioned=True,
                 e2e=(e2e, hin.numel() * 2, ho.numel() * 2),
                 kernel="decode_attn_kernel (fused NVLink exchange)", status=ws.status, allgather=allgather,
-                keep=(kc, vc, table, qv, kn, vn, out, ws, group, a, packed),
-                config={"seq_len": S, "page_size": P, "num_heads": H, "num_kv_heads": Hkv, "head_dim": d,
-                        "ranks": world, "shard_tokens_rank0": cpm.shard_tokens(S, P, world)[0][1],
+                keep=(kcs, vcs, tables, ins, outs, ws, group, args, packed),
+                config={"seq_len": S, "layers": layers, "page_size": P, "num_heads": H, "num_kv_heads": Hkv,
+                        "head_dim": d, "ranks": world, "shard_tokens_rank0": cpm.shard_tokens(S, P, world)[0][1],
                         "exchange": "in-kernel NVLink stores + system-scope flags, log-sum-exp merge"})
 
 
@@ -510,7 +517,8 @@ def partitioned_summary(wl, args, world, local, peaks):
     total = sum_over_ranks(float(wl["bytes"]), world)
     per_rank_gbs = wl["bytes"] / (ms * 1e-3) / 1e9
     res = {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
-           "us_per_step": round(ms * 1000, 2), "bytes_total": int(total),
+           "us_per_step": round(ms * 1000, 2), "us_per_layer": round(ms * 1000 / wl["launches"], 2),
+           "bytes_total": int(total),
            "e2e": {"value": round(total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                    "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2]},
            "rank0_frac_of_hbm": round(per_rank_gbs / peaks["hbm_gbs"], 4), "scaling": "strong",
@@ -519,6 +527,7 @@ def partitioned_summary(wl, args, world, local, peaks):
         ms_ag = time_eager(wl["allgather"], args.steps, args.warmup, world)
         res["allgather_nccl_path"] = {"value": round(total / (ms_ag * 1e-3) / 1e9, 2), "unit": "GB/s",
                                       "us_per_step": round(ms_ag * 1000, 2),
+                                      "us_per_layer": round(ms_ag * 1000 / wl["launches"], 2),
                                       "what": "partial kernel + NCCL all_gather_into_tensor + merge kernel"}
     return res, ms, ms_e2e, clocks
 

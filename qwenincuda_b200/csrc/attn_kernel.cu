@@ -284,47 +284,63 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   // RoPE position of q and of the appended k: the last attended token, or the
   // caller's global position when this launch holds one shard of a longer sequence
   const int rpos = (p.plan == nullptr && p.rope_pos >= 0) ? static_cast<int>(p.rope_pos) : S - 1;
+  // Before the preceding kernel has completed: the norm weights (constants) and the
+  // page-table entry of the appended row. The q rows go to warp w (rows w and w+4),
+  // the append to a warp with the fewest q rows; each warp issues all its row loads
+  // before it computes, so its prologue costs one load round trip.
+  const bool fuse_q = (p.flags & QIC_FUSE_Q_PROLOGUE) != 0;
+  const bool my_append = do_append && warp == G % kConsumerWarps;
+  float qw[D / 32], kw[D / 32];
+  if (fuse_q) row_load<T, D>(static_cast<const T*>(p.q_norm_w), qw, lane);
+  long long app_slot = S - 1;  // K/V append at position S-1 (src/model.cpp:634,637,639-641)
+  if (my_append) {
+    row_load<T, D>(static_cast<const T*>(p.k_norm_w), kw, lane);
+    if (table != nullptr) {
+      const int pos = S - 1, e = pos / p.page_size;
+      app_slot = static_cast<long long>(__ldg(table + e)) * p.page_size + (pos - e * p.page_size);
+    }
+  }
+  const bool app_ok = app_slot >= 0 && app_slot < p.cache_tokens;
   // inputs written by the preceding kernel are read only after it has completed
   pdl_wait();
   // ---- prologue: q rows into shared memory, and the fused append ----
   {
-    const int nrows = G + (do_append ? 1 : 0);
-#pragma unroll 1
-    for (int r = warp; r < nrows; r += kConsumerWarps) {
-      float v[D / 32];
-      if (r < G) {
-        row_load<T, D>(qb + static_cast<size_t>(kvh * G + r) * qhs, v, lane);
-        if (p.flags & QIC_FUSE_Q_PROLOGUE) {
-          row_rmsnorm<T, D>(v, static_cast<const T*>(p.q_norm_w), hd, p.eps, lane);
-          row_rope<T, D>(v, hd, rpos, p.theta, lane);
-        }
-        row_store<T, D>(q_s + r * D, v, lane);
-      } else {
-        // K/V append at position S-1 (src/model.cpp:634,637,639-641)
-        const int pos = S - 1;
-        long long slot = pos;
-        if (table != nullptr) {
-          const int e = pos / p.page_size;
-          slot = static_cast<long long>(__ldg(table + e)) * p.page_size + (pos - e * p.page_size);
-        }
-        const size_t kv_dim = static_cast<size_t>(p.Hkv) * D;
-        const size_t nb = static_cast<size_t>(b) * p.kv_new_bstride + static_cast<size_t>(kvh) * D;
-        if (slot >= 0 && slot < p.cache_tokens) {
-          row_load<T, D>(static_cast<const T*>(p.k_new) + nb, v, lane);
-          float vv[D / 32];
-          row_load<T, D>(static_cast<const T*>(p.v_new) + nb, vv, lane);
-          row_rmsnorm<T, D>(v, static_cast<const T*>(p.k_norm_w), hd, p.eps, lane);
-          row_rope<T, D>(v, hd, rpos, p.theta, lane);
-          const size_t at = static_cast<size_t>(slot) * kv_dim + static_cast<size_t>(kvh) * D;
-          row_store<T, D>(static_cast<T*>(p.k_cache) + at, v, lane);
-          row_store<T, D>(static_cast<T*>(p.v_cache) + at, vv, lane);
-        } else if (lane == 0) {
-          record_status(p.status, QIC_DEV_BAD_PAGE);
-        }
-        // the stage holding this row is copied by TMA (async proxy) after the barrier below
-        fence_proxy_async_global();
-        __syncwarp();
+    const int r0 = warp, r1 = warp + kConsumerWarps;  // G <= 8
+    float v0[D / 32], v1[D / 32], kr[D / 32], vr[D / 32];
+    const size_t nb = static_cast<size_t>(b) * p.kv_new_bstride + static_cast<size_t>(kvh) * D;
+    if (r0 < G) row_load<T, D>(qb + static_cast<size_t>(kvh * G + r0) * qhs, v0, lane);
+    if (r1 < G) row_load<T, D>(qb + static_cast<size_t>(kvh * G + r1) * qhs, v1, lane);
+    if (my_append && app_ok) {
+      row_load<T, D>(static_cast<const T*>(p.k_new) + nb, kr, lane);
+      row_load<T, D>(static_cast<const T*>(p.v_new) + nb, vr, lane);
+    }
+    if (r0 < G) {
+      if (fuse_q) {
+        row_rmsnorm_w<T, D>(v0, qw, hd, p.eps);
+        row_rope<T, D>(v0, hd, rpos, p.theta, lane);
       }
+      row_store<T, D>(q_s + r0 * D, v0, lane);
+    }
+    if (r1 < G) {
+      if (fuse_q) {
+        row_rmsnorm_w<T, D>(v1, qw, hd, p.eps);
+        row_rope<T, D>(v1, hd, rpos, p.theta, lane);
+      }
+      row_store<T, D>(q_s + r1 * D, v1, lane);
+    }
+    if (my_append) {
+      if (app_ok) {
+        row_rmsnorm_w<T, D>(kr, kw, hd, p.eps);
+        row_rope<T, D>(kr, hd, rpos, p.theta, lane);
+        const size_t at = static_cast<size_t>(app_slot) * static_cast<size_t>(p.Hkv) * D + static_cast<size_t>(kvh) * D;
+        row_store<T, D>(static_cast<T*>(p.k_cache) + at, kr, lane);
+        row_store<T, D>(static_cast<T*>(p.v_cache) + at, vr, lane);
+      } else if (lane == 0) {
+        record_status(p.status, QIC_DEV_BAD_PAGE);
+      }
+      // the stage holding this row is copied by TMA (async proxy) after the barrier below
+      fence_proxy_async_global();
+      __syncwarp();
     }
   }
   consumer_sync();

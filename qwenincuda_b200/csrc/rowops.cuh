@@ -83,20 +83,28 @@ __device__ __forceinline__ float row_sumsq_ordered(const float (&v)[D / 32]) {
   return s;
 }
 
-// In place: v = T(v * rsqrt(mean(v^2) + eps) * w).
+// In place: v = T(v * rsqrt(mean(v^2) + eps) * w), with this lane's weights wv
+// already loaded (row_load layout).
 template <typename T, int D>
-__device__ __forceinline__ void row_rmsnorm(float (&v)[D / 32], const T* __restrict__ w, int head_dim, float eps,
-                                            int lane) {
+__device__ __forceinline__ void row_rmsnorm_w(float (&v)[D / 32], const float (&wv)[D / 32], int head_dim,
+                                              float eps) {
   constexpr int E = D / 32;
   float ssum = row_sumsq_ordered<D>(v);
   float inv_rms = rsqrtf(ssum / static_cast<float>(head_dim) + eps);
-  float wv[E];
-  row_load<T, D>(w, wv, lane);
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     float xv = v[e];
     v[e] = to_f32<T>(from_f32<T>(xv * inv_rms * wv[e]));
   }
+}
+
+// In place: v = T(v * rsqrt(mean(v^2) + eps) * w).
+template <typename T, int D>
+__device__ __forceinline__ void row_rmsnorm(float (&v)[D / 32], const T* __restrict__ w, int head_dim, float eps,
+                                            int lane) {
+  float wv[D / 32];
+  row_load<T, D>(w, wv, lane);
+  row_rmsnorm_w<T, D>(v, wv, head_dim, eps);
 }
 
 // In place rotate-half RoPE at `position`: pairs (i, i + D/2). Lanes 0..15 hold the

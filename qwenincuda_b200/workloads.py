@@ -6,7 +6,9 @@ distributions of the configurations below.
 
   qwen3_0p6b_s1025   16 q heads, 8 kv heads, d=128, 1024 cached + append at 1024
                      (S=1025); K/V ~ N(0,1)*0.5; q/k head-RMSNormed (weight 1) then
-                     RoPE theta=1e6; page 16, table = seeded permutation of 65 pages
+                     RoPE theta=1e6; page 16, table = seeded permutation of 65 pages;
+                     32 layers, each with its own cache (the model has 28; 32 make a
+                     step's 134 MB of K/V larger than L2)
   qwen3_8b_s8192     36 layers, 32 q heads, 8 kv heads, d=128; stacked cache
                      [36, 8192, 8*128] ~ N(0, 0.5^2); append at 8191, S=8192;
                      contiguous and paged (page 16, shuffled table per layer)
@@ -64,7 +66,7 @@ class AttnConfig:
 
 
 CONFIGS = {
-    "qwen3_0p6b_s1025": AttnConfig("qwen3_0p6b_s1025", 16, 8, 128, 1025, kv_std=0.5, seed=1),
+    "qwen3_0p6b_s1025": AttnConfig("qwen3_0p6b_s1025", 16, 8, 128, 1025, layers=32, kv_std=0.5, seed=1),
     "qwen3_8b_s8192": AttnConfig("qwen3_8b_s8192", 32, 8, 128, 8192, layers=36, seed=2),
     "qwen35_gated_s32769": AttnConfig("qwen35_gated_s32769", 16, 4, 256, 32769, layers=8, gate=True, seed=3),
     "qwen3_8b_s131073": AttnConfig("qwen3_8b_s131073", 32, 8, 128, 131073, seed=4),
