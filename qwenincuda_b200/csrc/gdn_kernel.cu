@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   __shared__ float red[kGdnThreads / 32][NC];
   __shared__ float col_s[NC];
   __shared__ float scal[4];
-  __shared__ float ssq_part;  // read by the other CTAs of this value head
+  __shared__ float ssq_all[CB];  // the value head's CB partial sums of squares, pushed by their CTAs
 
   const T* qkv = static_cast<const T*>(a.qkv);
   const T* conv_w = static_cast<const T*>(a.conv_w);
@@ -240,16 +240,22 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   block_colsum(part);  // col_s = o for this CTA's columns
 
   // ---- 6. gated RMSNorm over the value head's 128 columns (src/model.cpp:777-791) ----
+  float ss_mine = 0.0f;  // this CTA's sum of squares (warp 0)
   if (tid < 32) {
     float ss = 0.0f;
     for (int j = tid; j < NC; j += 32) ss = __fadd_rn(ss, __fmul_rn(col_s[j], col_s[j]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (tid == 0) ssq_part = ss;
+    ss_mine = ss;
   }
-  // every CTA has read the old conv state: write the new one (q/k channels by the
-  // first value head's CTAs, v channels by their owner)
+  // every CTA of the cluster is running and has read the old conv state
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+  // this CTA's partial goes into slot cb of every CTA of its value head (DSMEM stores
+  // before the cluster barrier below), so after that barrier every CTA reads only its
+  // own shared memory and may exit without waiting for its peers
+  if (tid < CB) *cluster.map_shared_rank(&ssq_all[cb], vloc * CB + tid) = ss_mine;
+  // the new conv state (q/k channels by the first value head's CTAs, v channels by
+  // their owner)
   if (vloc == 0) {
     constexpr int QK_PER = kGdnDk / CB;
     if (tid >= cb * QK_PER && tid < (cb + 1) * QK_PER) {
@@ -268,13 +274,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
       if (t < K) conv_state[static_cast<size_t>(cv) * K + t] = win_v[t];
     }
   }
-  cluster.sync();  // every CTA's ssq_part is written
+  cluster.sync();  // every partial of this value head is in ssq_all
   float ss = 0.0f;
 #pragma unroll
-  for (int c = 0; c < CB; ++c) {
-    const float* remote = cluster.map_shared_rank(&ssq_part, vloc * CB + c);
-    ss += *remote;
-  }
+  for (int c = 0; c < CB; ++c) ss += ssq_all[c];
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kGdnDv) + a.eps);
   if (tid < NC) {
     const int j = cb * NC + tid;
@@ -284,8 +287,6 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
     const float ww = to_f32<T>(nw_raw);
     static_cast<T*>(a.out)[static_cast<size_t>(vh) * kGdnDv + j] = from_f32<T>(__fmul_rn(__fmul_rn(normed, ww), gate));
   }
-  // keep this CTA's shared memory alive until every peer has read ssq_part
-  cluster.sync();
 }
 
 template <typename T, int REP, int CB>
