@@ -52,7 +52,8 @@ enum {
   QIC_DEV_TIMEOUT = 1,           /* a bounded wait timed out */
   QIC_DEV_BAD_PAGE = 2,          /* an out-of-range page-table entry was clamped to page 0 */
   QIC_DEV_PEER_TIMEOUT = 4,      /* a peer never published its partial */
-  QIC_DEV_BAD_PLAN = 8           /* a batched work item does not fit the workspace; it was skipped */
+  QIC_DEV_BAD_PLAN = 8,          /* a batched work item does not fit the workspace; it was skipped */
+  QIC_DEV_BAD_LENGTH = 16        /* a device-resident sequence length was outside [1, seq_len]; clamped */
 };
 
 /* Flags of qic_decode_args.flags */
@@ -82,11 +83,20 @@ enum {
                                     of the sequence's stages to whichever CTA asks first (load
                                     balance), so the order in which split partials are summed, and the
                                     last bits of the output, can change from call to call. */
-  QIC_Q_GATE_INTERLEAVED = 64    /* q is the interleaved q/gate projection [H, 2d] (per head d q values,
+  QIC_Q_GATE_INTERLEAVED = 64,   /* q is the interleaved q/gate projection [H, 2d] (per head d q values,
                                     then d gate values) and out *= sigmoid(gate) with that gate; `gate`
                                     must be NULL. Folds launch_split_q_gate_interleaved
                                     (src/kernels.cu:113-127, src/model.cpp:628) into the kernel. Batched
                                     calls: q is [B, H, 2d]. Partial outputs carry no gate. */
+  QIC_DEVICE_SEQ_LEN = 128       /* the number of tokens attended is read from device memory
+                                    (args->seq_len_dev, an int32 in [1, args->seq_len]) when the kernel
+                                    starts; args->seq_len is the largest it may be and sizes the launch.
+                                    A decode loop captured once in a CUDA graph then replays for every
+                                    token: the caller advances the length (and any new page-table
+                                    entry) in device memory before each replay. The length is read
+                                    early like the page table (QIC_PDL). Needs a workspace (an
+                                    out-of-range length is clamped and reported as QIC_DEV_BAD_LENGTH);
+                                    not with context parallelism. */
 };
 
 const char* qic_status_string(int status);
@@ -156,6 +166,7 @@ typedef struct qic_decode_args {
   int32_t cluster_size;     /* splits merged on chip per thread-block cluster (1..16, divides
                                num_splits); 0 = chosen with num_splits */
   int64_t position;         /* QIC_EXPLICIT_POSITION: RoPE position of q and the appended k */
+  const int32_t* seq_len_dev; /* QIC_DEVICE_SEQ_LEN: device int32, the current seq_len */
 } qic_decode_args;
 
 /* Scratch bytes qic_decode_attention needs for this shape (any seq_len up to max_seq_len).

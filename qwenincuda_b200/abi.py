@@ -13,11 +13,13 @@ QIC_DEV_TIMEOUT = 1
 QIC_DEV_BAD_PAGE = 2
 QIC_DEV_PEER_TIMEOUT = 4
 QIC_DEV_BAD_PLAN = 8
+QIC_DEV_BAD_LENGTH = 16
 QIC_PDL = 4
 QIC_PARTIAL_OUT = 8
 QIC_EXPLICIT_POSITION = 16
 QIC_DETERMINISTIC = 32
 QIC_Q_GATE_INTERLEAVED = 64
+QIC_DEVICE_SEQ_LEN = 128
 QIC_MAX_RANKS = 8
 QIC_IPC_HANDLE_BYTES = 64
 
@@ -79,6 +81,7 @@ class DecodeArgs(ctypes.Structure):
         ("num_splits", ctypes.c_int32),
         ("cluster_size", ctypes.c_int32),
         ("position", ctypes.c_int64),
+        ("seq_len_dev", ctypes.c_void_p),
     ]
 
 

@@ -154,8 +154,20 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     split = blockIdx.x;
     nsplit = p.n_splits;
     S = p.seq_len;
-    st_lo = static_cast<int>(static_cast<long long>(split) * p.n_stages / nsplit);
-    st_hi = static_cast<int>(static_cast<long long>(split + 1) * p.n_stages / nsplit);
+    int nst = p.n_stages;
+    if (p.seq_len_dev != nullptr) {
+      // the current length, written before this launch like the page table; the launch
+      // is sized for p.seq_len, so a length outside [1, p.seq_len] is clamped into it
+      int sd = *p.seq_len_dev;
+      if (sd < 1 || sd > p.seq_len) {
+        if (threadIdx.x == 0) record_status(p.status, QIC_DEV_BAD_LENGTH);
+        sd = sd < 1 ? 1 : p.seq_len;
+      }
+      S = sd;
+      nst = (S + TOK - 1) / TOK;
+    }
+    st_lo = static_cast<int>(static_cast<long long>(split) * nst / nsplit);
+    st_hi = static_cast<int>(static_cast<long long>(split + 1) * nst / nsplit);
     part_base = kvh * (nsplit / p.cluster);  // one global slot per cluster
   }
   if (p.cluster == 1 && nsplit > 1 &&

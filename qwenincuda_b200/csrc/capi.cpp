@@ -269,6 +269,12 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
                                   a->q_norm_w, a->k_norm_w, a->k_new, a->v_new, a->workspace);
   if (rc != QIC_SUCCESS) return rc;
   if (S < 0) return QIC_ERROR_INVALID_VALUE;
+  // device-resident length: seq_len is its upper bound and sizes the launch
+  const bool dev_len = (a->flags & QIC_DEVICE_SEQ_LEN) != 0;
+  if (dev_len && (a->seq_len_dev == nullptr || (reinterpret_cast<uintptr_t>(a->seq_len_dev) & 3u) != 0 || S < 1 ||
+                  a->workspace == nullptr))
+    return QIC_ERROR_INVALID_VALUE;
+  if (dev_len && cp != nullptr) return QIC_ERROR_NOT_SUPPORTED;
   const int G = H / Hkv;
   const bool paged = a->page_table != nullptr;
   if (paged && (a->page_size <= 0 || a->page_size % 8 != 0)) return QIC_ERROR_NOT_SUPPORTED;
@@ -399,6 +405,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   p.log2_box_h = lbh;
   p.n_stages = n_stages;
   p.n_splits = n_splits;
+  p.seq_len_dev = dev_len ? a->seq_len_dev : nullptr;
   p.rope_pos = (a->flags & QIC_EXPLICIT_POSITION) ? a->position : -1;
   if (partial_out) p.part_out = static_cast<float*>(a->out);
   if (cp != nullptr) {

@@ -98,6 +98,7 @@ struct AttnParams {
   long long rope_pos;                // RoPE position of q and the appended k (single-sequence launches)
   float* part_out;                   // QIC_PARTIAL_OUT: [Hkv][partial_floats] instead of out
   int* stage_ctr;                    // per kv head ticket counters of the stage pool, or null
+  const int32_t* seq_len_dev;        // QIC_DEVICE_SEQ_LEN: the current length (seq_len is its bound), or null
   // context parallelism (cp_world == 0: off)
   int cp_rank, cp_world;
   int cp_mergers;                    // slice mergers per call on this rank: Hkv * kCpSlices

@@ -17,6 +17,7 @@ from .abi import (
     QIC_DTYPE_BF16,
     QIC_DTYPE_F16,
     QIC_DETERMINISTIC,
+    QIC_DEVICE_SEQ_LEN,
     QIC_EXPLICIT_POSITION,
     QIC_FUSE_APPEND,
     QIC_FUSE_Q_PROLOGUE,
@@ -108,13 +109,14 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
                 page_size=16, gate=None, q_norm_w=None, k_norm_w=None, k_new=None, v_new=None, eps=1e-6,
                 rope_theta=1.0e6, fuse_q=False, fuse_append=False, workspace=None, num_splits=0,
                 cache_tokens=None, pdl=False, cluster_size=0, position=None, partial_out=False,
-                deterministic=False, q_gate_interleaved=False) -> DecodeArgs:
+                deterministic=False, q_gate_interleaved=False, seq_len_dev=None) -> DecodeArgs:
     """qic_decode_args for one call. position: RoPE position of q and the appended k
     (default seq_len - 1). partial_out: `out` is an fp32 tensor of
     num_kv_heads * partial_floats(...) elements receiving the (o, lse) partial.
     deterministic: bitwise-reproducible outputs (no dynamic stage pool).
     q_gate_interleaved: q is the [H, 2d] q/gate projection and out is gated by its
-    second halves (gate must be None)."""
+    second halves (gate must be None). seq_len_dev: a device int32 tensor holding the
+    current length, read when the kernel starts (seq_len is then its upper bound)."""
     a = DecodeArgs()
     a.dtype = dtype_code(k_cache)
     a.num_heads = num_heads
@@ -135,6 +137,11 @@ def decode_args(*, q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, 
         a.position = int(position)
     if deterministic:
         a.flags |= QIC_DETERMINISTIC
+    if seq_len_dev is not None:
+        if seq_len_dev.dtype != torch.int32 or not seq_len_dev.is_cuda:
+            raise TypeError("seq_len_dev is a CUDA int32 tensor")
+        a.flags |= QIC_DEVICE_SEQ_LEN
+        a.seq_len_dev = seq_len_dev.data_ptr()
     if partial_out:
         if out.dtype != torch.float32:
             raise TypeError("a partial output is float32")

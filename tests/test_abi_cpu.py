@@ -103,6 +103,13 @@ def test_argument_validation_without_device():
     a.flags = q.abi.QIC_Q_GATE_INTERLEAVED
     a.gate = 0x30000
     assert L.qic_decode_attention(ctypes.byref(a), None) == 1          # gate given twice (interleaved q)
+    a.flags = q.abi.QIC_DEVICE_SEQ_LEN
+    a.gate = None
+    assert L.qic_decode_attention(ctypes.byref(a), None) == 1          # device length without its pointer
+    a.seq_len_dev = 0x40002
+    assert L.qic_decode_attention(ctypes.byref(a), None) == 1          # misaligned length pointer
+    a.seq_len_dev = 0x40000
+    assert L.qic_decode_attention(ctypes.byref(a), None) == 1          # device length without a workspace
 
 
 def test_header_constants_match_bindings():
@@ -130,3 +137,30 @@ def test_libraries_bind_their_own_symbols():
     for p in libs:
         out = subprocess.run(["readelf", "-d", str(p)], capture_output=True, text=True, check=True).stdout
         assert "SYMBOLIC" in out, p
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """Every ctypes mirror has the C struct's size and every field its C offset: a C
+    program compiled against include/qic.h prints them (gcc, no GPU)."""
+    from qwenincuda_b200 import abi
+
+    mirrors = {"qic_decode_args": abi.DecodeArgs, "qic_cp_args": abi.CpArgs,
+               "qic_batch_decode_args": abi.BatchDecodeArgs, "qic_gdn_args": abi.GdnArgs}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "qic.h"', "int main(void) {"]
+    for cname, cls in mirrors.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        cname, field, value = line.split()
+        got[(cname, field)] = int(value)
+    for cname, cls in mirrors.items():
+        assert ctypes.sizeof(cls) == got[(cname, "sizeof")], cname
+        for field, _ in cls._fields_:
+            assert getattr(cls, field).offset == got[(cname, field)], f"{cname}.{field}"

@@ -345,3 +345,126 @@ def test_interleaved_q_gate_rejects_a_second_gate():
     with pytest.raises(RuntimeError, match="INVALID_VALUE"):
         q.decode_attention(q=packed, gate=qv, k_cache=kc, v_cache=vc, out=out, num_heads=H, num_kv_heads=Hkv,
                            head_dim=d, seq_len=S, q_gate_interleaved=True)
+
+
+def _dev_len_case(S_max, seed, dtype=torch.bfloat16):
+    """Paged K/V for S_max tokens, raw q / k_new / v_new and norm weights."""
+    H, Hkv, d, P = 32, 8, 128, 16
+    qv, kc, vc, table = _inputs(H, Hkv, d, S_max, P, dtype, seed)
+    g = _gen(seed + 1)
+    kn = torch.randn(Hkv * d, generator=g, device="cuda").to(dtype)
+    vn = (torch.randn(Hkv * d, generator=g, device="cuda") * 0.5).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(dtype)
+    return (H, Hkv, d, P), dict(q=qv, k_cache=kc, v_cache=vc, page_table=table, page_size=P, q_norm_w=w, k_norm_w=w,
+                                k_new=kn, v_new=vn, num_heads=H, num_kv_heads=Hkv, head_dim=d, fuse_q=True,
+                                fuse_append=True, num_splits=16, cluster_size=8, deterministic=True)
+
+
+@pytest.mark.parametrize("S", [1, 33, 1025, 4097])
+def test_device_seq_len_matches_host_length(S):
+    """QIC_DEVICE_SEQ_LEN: the length read from device memory by a launch sized for
+    6000 tokens gives the same bytes (outputs and the appended rows) as the same
+    launch shape with the length passed by value."""
+    S_max = 6000
+    (H, Hkv, d, P), kw = _dev_len_case(S_max, seed=71)
+    kc0, vc0 = kw["k_cache"].clone(), kw["v_cache"].clone()
+    outs, caches = [], []
+    for dev in (False, True):
+        kk = dict(kw, k_cache=kc0.clone(), v_cache=vc0.clone())
+        out = torch.full((H * d,), float("nan"), device="cuda", dtype=torch.bfloat16)
+        ws = q.Workspace(H, Hkv, d, S_max)
+        if dev:
+            q.decode_attention(out=out, seq_len=S_max, seq_len_dev=torch.tensor([S], dtype=torch.int32, device="cuda"),
+                               workspace=ws, **kk)
+        else:
+            q.decode_attention(out=out, seq_len=S, workspace=ws, **kk)
+        torch.cuda.synchronize()
+        assert ws.status() == 0
+        outs.append(out)
+        caches.append((kk["k_cache"], kk["v_cache"]))
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    for a, b in zip(caches[0], caches[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    want = _ref(*_reference_q(kw, S), caches[0][0], caches[0][1], H, Hkv, d, S, kw["page_table"], P)
+    ok, err, idx = allclose_report(outs[1], want, ATOL, RTOL)
+    assert ok, f"max abs err {err} at {idx}"
+
+
+def _reference_q(kw, S):
+    """q after the reference's head-RMSNorm and RoPE at position S-1."""
+    ref = RefKernels(kw["q"].dtype)
+    qq = kw["q"].clone()
+    ref.head_rmsnorm(qq, kw["q_norm_w"], kw["num_heads"], kw["head_dim"], 1e-6, qq)
+    ref.rope_inplace(qq, kw["num_heads"], kw["head_dim"], S - 1, 1.0e6)
+    return (qq,)
+
+
+def test_device_seq_len_graph_replays_a_decode_loop():
+    """One fused decode call captured once in a CUDA graph and replayed for four
+    successive tokens (the length advanced in device memory and the token's q, k_new,
+    v_new copied in before each replay) gives the same outputs and cache bytes as four
+    calls with the length passed by value."""
+    S0, S_max, steps = 1000, 1100, 4
+    (H, Hkv, d, P), kw = _dev_len_case(S_max, seed=73)
+    g = _gen(74)
+    toks = [(torch.randn(H * d, generator=g, device="cuda").to(torch.bfloat16),
+             torch.randn(Hkv * d, generator=g, device="cuda").to(torch.bfloat16),
+             (torch.randn(Hkv * d, generator=g, device="cuda") * 0.5).to(torch.bfloat16)) for _ in range(steps)]
+    kc0, vc0 = kw["k_cache"].clone(), kw["v_cache"].clone()
+    # by value
+    kc, vc = kc0.clone(), vc0.clone()
+    ws = q.Workspace(H, Hkv, d, S_max)
+    want = []
+    for t, (qt, kt, vt) in enumerate(toks):
+        out = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+        q.decode_attention(out=out, seq_len=S0 + t, workspace=ws, **dict(kw, q=qt, k_new=kt, v_new=vt, k_cache=kc,
+                                                                          v_cache=vc))
+        want.append(out)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    # one graph, replayed
+    kg, vg = kc0.clone(), vc0.clone()
+    qb, kb, vb = (torch.empty_like(x) for x in toks[0])
+    length = torch.tensor([S0], dtype=torch.int32, device="cuda")
+    out_g = torch.empty(H * d, device="cuda", dtype=torch.bfloat16)
+    wsg = q.Workspace(H, Hkv, d, S_max)
+    args = dict(kw, q=qb, k_new=kb, v_new=vb, k_cache=kg, v_cache=vg)
+    # the first call on a device does per-device set-up: make it outside the capture,
+    # on copies of the caches
+    q.decode_attention(out=out_g, seq_len=S_max, seq_len_dev=length, workspace=wsg,
+                       **dict(args, k_cache=kc0.clone(), v_cache=vc0.clone()))
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        q.decode_attention(out=out_g, seq_len=S_max, seq_len_dev=length, workspace=wsg, **args)
+    got = []
+    for t, (qt, kt, vt) in enumerate(toks):
+        length.fill_(S0 + t)
+        qb.copy_(qt)
+        kb.copy_(kt)
+        vb.copy_(vt)
+        graph.replay()
+        got.append(out_g.clone())
+    torch.cuda.synchronize()
+    assert wsg.status() == 0
+    for t in range(steps):
+        assert torch.equal(got[t].view(torch.int16), want[t].view(torch.int16)), f"token {t}"
+    assert torch.equal(kg.view(torch.int16), kc.view(torch.int16))
+    assert torch.equal(vg.view(torch.int16), vc.view(torch.int16))
+
+
+def test_device_seq_len_out_of_range_is_clamped_and_reported():
+    """A device length outside [1, seq_len] is clamped into it (every access stays
+    inside the launch's bounds) and reported in the status word."""
+    S_max = 300
+    (H, Hkv, d, P), kw = _dev_len_case(S_max, seed=75)
+    kw = dict(kw, fuse_append=False)
+    ws = q.Workspace(H, Hkv, d, S_max)
+    for bad in (0, -5, S_max + 7):
+        out = torch.full((H * d,), float("nan"), device="cuda", dtype=torch.bfloat16)
+        q.decode_attention(out=out, seq_len=S_max, seq_len_dev=torch.tensor([bad], dtype=torch.int32, device="cuda"),
+                           workspace=ws, **kw)
+        torch.cuda.synchronize()
+        assert ws.status() & q.abi.QIC_DEV_BAD_LENGTH, bad
+        assert torch.isfinite(out.float()).all(), bad
+    assert ws.status() == 0
