@@ -24,18 +24,24 @@
 //    x 8 query-head columns); the online softmax runs in the exp2 domain on the
 //    fragments; P^T is turned into the B operand with movmatrix; O^T += V^T P
 //    accumulates in registers.
-//  * Fused options: the q prologue (head RMSNorm + RoPE of q), the K/V append of the
-//    new token (head RMSNorm + RoPE of k written into its page slot before the
-//    stage holding it is copied), and the sigmoid output gate.
+//  * Fused options: the q prologue (head RMSNorm + RoPE of q, read from q or from
+//    the interleaved q/gate projection), the K/V append of the new token (head
+//    RMSNorm + RoPE of k written into its page slot before the stage holding it is
+//    copied), and the sigmoid output gate.
 //  * The splits of a kv head form thread-block clusters. Each CTA leaves its (o, lse)
 //    partial in shared memory; after a cluster barrier every CTA merges one slice of
-//    the outputs from all partials of its cluster through distributed shared memory.
-//    When a kv head spans several clusters, each cluster slice is written to the
-//    caller's workspace and the last arriving CTA of that slice (release/acquire
-//    counter) merges the cluster partials by log-sum-exp.
+//    the outputs from all partials of its cluster through distributed shared memory,
+//    then arrives (relaxed) at the second barrier phase, whose wait is the kernel's
+//    last instruction. When a kv head spans several clusters, each cluster slice is
+//    written to the caller's workspace and the last arriving CTA of that slice
+//    (release/acquire counter) merges the cluster partials by log-sum-exp.
+//  * Long sequences hand out their first eighth of stages one at a time (a per-kv-head
+//    ticket counter in the workspace) to the warps that finish their own range first.
 //  * Programmatic dependent launch (QIC_PDL): the CTA signals its dependents at
-//    start and reads its inputs, the append slot and the workspace only after
-//    griddepcontrol.wait, so the next call's K/V prefetch overlaps this call's tail.
+//    start; the norm weights, page-table entries, cached K/V rows and a device-resident
+//    length (QIC_DEVICE_SEQ_LEN) are read before griddepcontrol.wait, q, k_new,
+//    v_new, the gate and the workspace after it, so the next call's K/V prefetch
+//    overlaps this call's tail.
 //  * Every wait is bounded (ptx.cuh); on timeout the CTA records QIC_DEV_TIMEOUT,
 //    drains its own copies (bounded) and exits.
 //
