@@ -40,8 +40,9 @@
 //  * Programmatic dependent launch (QIC_PDL): the CTA signals its dependents at
 //    start; the norm weights, page-table entries, cached K/V rows and a device-resident
 //    length (QIC_DEVICE_SEQ_LEN) are read before griddepcontrol.wait, q, k_new,
-//    v_new, the gate and the workspace after it, so the next call's K/V prefetch
-//    overlaps this call's tail.
+//    v_new, the gate and the workspace's counters and partials after it (a bad page
+//    or length may be OR-ed into the status word before it), so the next call's K/V
+//    prefetch overlaps this call's tail.
 //  * Every wait is bounded (ptx.cuh); on timeout the CTA records QIC_DEV_TIMEOUT,
 //    drains its own copies (bounded) and exits.
 //
