@@ -7,6 +7,10 @@
   reference's own src/kernels.cu compiled unchanged for sm_100a (oracle/Makefile).
   Takes CUDA torch tensors; launches on the legacy default stream like the
   reference and synchronises.
+* ``RefGatedDelta``: ctypes binding of oracle/_ref/libqicref_gdn.so, the reference's
+  own GatedDeltaNet decode step (src/model.cpp:656-795, compiled unchanged inside
+  oracle/ref_gdn_harness.cpp). Takes and returns CPU tensors (fp16 inputs, fp32
+  states); needs a CUDA device, through which the reference copies its inputs.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs
 use this module; the product library never does.
@@ -216,3 +220,36 @@ class RefKernels:
         self._chk(self.lib.qicref_copy_row(_p(v_cache), _p(v_new), slot, kv_dim), "copy v")
         self.sync()
         return k
+
+
+class RefGatedDelta:
+    """The reference's own GatedDeltaNet decode step (run_linear_attention_block,
+    src/model.cpp:656-795), fp16 as the reference ships it."""
+
+    def __init__(self):
+        path = REF_DIR / "libqicref_gdn.so"
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
+        lib.qicref_gdn_step.argtypes = [_i, _i, _i, _i, _i, _f] + [_vp] * 11
+        lib.qicref_gdn_step.restype = _i
+        self.lib = lib
+
+    @staticmethod
+    def available() -> bool:
+        return (REF_DIR / "libqicref_gdn.so").exists()
+
+    def step(self, *, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, num_k_heads,
+             num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6):
+        """Returns (out, new conv_state, new recurrent_state); inputs are not modified."""
+        ins = [_cpu(t) for t in (qkv, z, b, a, conv_w, dt_bias, a_log, norm_w)]
+        if any(t.dtype != torch.float16 for t in ins):
+            raise TypeError("the reference's GatedDeltaNet step is fp16")
+        cs = _cpu(conv_state).float().clone()
+        rs = _cpu(recurrent_state).float().clone()
+        out = torch.empty(num_v_heads * v_head_dim, dtype=torch.float16)
+        rc = self.lib.qicref_gdn_step(num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps,
+                                      *[_p(t) for t in ins], _p(cs), _p(rs), _p(out))
+        if rc != 0:
+            raise RuntimeError("reference GatedDeltaNet step failed")
+        return out, cs, rs

@@ -63,3 +63,35 @@ def test_gdn_pdl_chain_matches_plain_launches(layers):
     for l, (plain, chained) in enumerate(zip(*results)):
         for name, x, y in zip(("out", "conv_state", "recurrent_state"), plain, chained):
             assert torch.equal(x, y), f"layer {l} {name}"
+
+
+def test_gdn_kernel_vs_reference_step():
+    """The CUDA kernel against the reference's own decode step (run_linear_attention_block,
+    src/model.cpp:656-795, run unchanged through oracle/_ref/libqicref_gdn.so) on fp16
+    inputs over three steps carrying the states: output within max-abs 2e-3 / rel 1e-2,
+    conv state exact, recurrent state within fp32 rounding."""
+    from oracle.oracle import RefGatedDelta
+
+    ref = RefGatedDelta()
+    Hk, Hv = 4, 8
+    cfg = GdnConfig(num_k_heads=Hk, num_v_heads=Hv)
+    dev = make_gdn_inputs(cfg, device="cuda", dtype=torch.float16)
+    host = {k: v.cpu().clone() for k, v in dev.items()}
+    g = torch.Generator(device="cuda").manual_seed(78)
+    for step in range(3):
+        if step:
+            for k, n in (("qkv", cfg.conv_dim), ("z", Hv * 128), ("b", Hv), ("a", Hv)):
+                new = torch.randn(n, generator=g, device="cuda").to(torch.float16)
+                dev[k].copy_(new)
+                host[k] = new.cpu()
+        q.gated_delta_decode(**dev, num_k_heads=Hk, num_v_heads=Hv)
+        torch.cuda.synchronize()
+        want_out, want_cs, want_rs = ref.step(**{k: host[k] for k in host if k != "out"}, num_k_heads=Hk,
+                                              num_v_heads=Hv, eps=cfg.eps)
+        host["conv_state"], host["recurrent_state"] = want_cs.view_as(host["conv_state"]), \
+            want_rs.view_as(host["recurrent_state"])
+        assert torch.equal(dev["conv_state"].cpu(), host["conv_state"]), f"conv state step {step}"
+        ok, err, _ = allclose_report(dev["recurrent_state"], host["recurrent_state"], atol=1e-5, rtol=1e-4)
+        assert ok, f"state step {step}: {err}"
+        ok, err, idx = allclose_report(dev["out"], want_out)
+        assert ok, f"out step {step}: {err} at {idx}"

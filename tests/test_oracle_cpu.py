@@ -192,5 +192,20 @@ def test_oracle_against_reference_golden(oracle, path):
         got = oracle.sigmoid_mul(case["x"], case["gate"])
         ok, err, _ = allclose_report(got, case["out"], atol=0, rtol=2 ** -7)
         assert ok, err
+    elif kind == "gated_delta":
+        # the reference's own host loop (tests/golden/make_gdn_golden.py): the
+        # restatement follows it operation for operation in IEEE fp32, so every step's
+        # output and both final states are bit-identical
+        Hk, Hv, dk, dv, K, _ = case["case"]
+        inp = case["inputs"]
+        cs, rs = inp["conv_state"], inp["recurrent_state"]
+        for t, st in enumerate(inp["steps"]):
+            got, cs, rs = oracle.gated_delta(**st, conv_w=inp["conv_w"], dt_bias=inp["dt_bias"], a_log=inp["a_log"],
+                                             norm_w=inp["norm_w"], conv_state=cs, recurrent_state=rs, num_k_heads=Hk,
+                                             num_v_heads=Hv, k_head_dim=dk, v_head_dim=dv, conv_kernel=K,
+                                             eps=case["eps"])
+            assert torch.equal(got.view(torch.int16), case["outs"][t].view(torch.int16)), f"output, step {t}"
+        assert torch.equal(cs, case["conv_state"])
+        assert torch.equal(rs, case["recurrent_state"])
     else:
         pytest.fail(f"unknown golden kind {kind}")
