@@ -30,10 +30,12 @@ qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64 (64 sequen
 lengths 512..32768, one shared page pool, one batched launch).
 
 --impl reference (rank 0 only): the reference's implementation of the same workload
-on the host cores, as the line's value: the oracle's C restatement of src/kernels.cu's
-paged attention and of the GatedDeltaNet host loop (src/model.cpp:692-793), OpenMP
-over heads, on a bounded sample. For the attention workloads the reference's own
-kernels built for sm_100a are also timed on the GPU.
+on the host cores, as the line's value, on a bounded sample. Attention: the oracle's C
+restatement of src/kernels.cu's paged attention, OpenMP over heads (the reference has
+no CPU attention), and the reference's own kernels built for sm_100a timed on the GPU
+as extra information. GatedDeltaNet: the reference's own step, whose loop runs on the
+host (run_linear_attention_block, src/model.cpp:656-795, built unchanged into
+oracle/_ref), or the oracle's restatement of it when that library is absent.
 """
 from __future__ import annotations
 
@@ -593,7 +595,24 @@ def cpu_baseline(workload, budget_s=6.0):
         return run, cfg.kv_read_bytes() + cfg.append_bytes(), f"paged attention at S={S} (H={H}, Hkv={Hkv}, d={d})"
 
     def gdn_step():
+        """The reference's own step (its host loop with its device copies, fp16 as it
+        ships, one host thread) when oracle/_ref holds it and a GPU is present, else
+        the oracle's restatement (OpenMP)."""
+        from oracle.oracle import RefGatedDelta
+
         cfg = GdnConfig()
+        what = f"GatedDeltaNet decode (Hk={cfg.num_k_heads}, Hv={cfg.num_v_heads}, d=128)"
+        if RefGatedDelta.available() and torch.cuda.is_available():
+            t = make_gdn_inputs(cfg, device="cpu", dtype=torch.float16)
+            layer = RefGatedDelta().layer(conv_w=t["conv_w"], dt_bias=t["dt_bias"], a_log=t["a_log"],
+                                          norm_w=t["norm_w"], conv_state=t["conv_state"],
+                                          recurrent_state=t["recurrent_state"], num_k_heads=cfg.num_k_heads,
+                                          num_v_heads=cfg.num_v_heads, conv_kernel=cfg.conv_kernel, eps=cfg.eps)
+            layer.run(qkv=t["qkv"], z=t["z"], b=t["b"], a=t["a"])  # the step's projections, uploaded once
+            keep.append(layer)
+            return (layer.run, cfg.state_bytes(), "reference", 1,
+                    what + " through the reference's run_linear_attention_block (src/model.cpp:656-795: cuBLAS "
+                    "projections, 8 device-to-host copies, host loop, 1 copy back), fp16, one host thread")
         t = make_gdn_inputs(cfg, device="cpu")
         kw = {k: t[k] for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state",
                                 "recurrent_state")}
@@ -602,23 +621,26 @@ def cpu_baseline(workload, budget_s=6.0):
             orc.gated_delta(num_k_heads=cfg.num_k_heads, num_v_heads=cfg.num_v_heads, conv_kernel=cfg.conv_kernel,
                             eps=cfg.eps, **kw)
 
-        return run, cfg.state_bytes(), f"GatedDeltaNet decode (Hk={cfg.num_k_heads}, Hv={cfg.num_v_heads}, d=128)"
+        return run, cfg.state_bytes(), "port", threads, what + " (oracle restatement)"
 
+    keep = []  # reference layers held open while timed
+    kind, cores = "port", threads
     if workload in ATTN_WORKLOADS:
         run, nbytes, what = attention_layer(CONFIGS[workload])
         unit_name = "layers"
     elif workload == "qwen35_gdn":
-        run, nbytes, what = gdn_step()
+        run, nbytes, kind, cores, what = gdn_step()
         unit_name = "steps"
     elif workload == "qwen35_pair":
-        g_run, g_bytes, _ = gdn_step()
+        g_run, g_bytes, g_kind, _, g_what = gdn_step()
         a_run, a_bytes, a_what = attention_layer(CONFIGS["qwen35_gated_s32769"])
 
         def run():
             g_run()
             a_run()
 
-        nbytes, what, unit_name = g_bytes + a_bytes, f"GatedDeltaNet step + gated {a_what}", "steps"
+        nbytes, what, unit_name = g_bytes + a_bytes, f"{g_what}, then gated {a_what} (oracle)", "steps"
+        kind = "reference + port" if g_kind == "reference" else "port"
     elif workload == "qwen3_8b_batch64":
         cfg = BatchConfig()
         lens = cfg.seq_lens()[:4]
@@ -639,9 +661,11 @@ def cpu_baseline(workload, budget_s=6.0):
     else:
         raise SystemExit(f"unknown workload {workload}")
     n, el = _timed_loop(run, budget_s)
+    for layer in keep:
+        layer.close()
     per = el / n
     return {"value": round(nbytes / per / 1e9, 3), "unit": "GB/s", f"us_per_{unit_name[:-1]}": round(per * 1e6, 1),
-            "cores": threads, "kind": "port", "sample": f"{n} {unit_name} of {what} in {el:.1f} s"}
+            "cores": cores, "kind": kind, "sample": f"{n} {unit_name} of {what} in {el:.1f} s"}
 
 
 def reference_gpu(cfg, layers, steps, warmup):

@@ -233,6 +233,12 @@ class RefGatedDelta:
         lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
         lib.qicref_gdn_step.argtypes = [_i, _i, _i, _i, _i, _f] + [_vp] * 11
         lib.qicref_gdn_step.restype = _i
+        lib.qicref_gdn_create.argtypes = [_i, _i, _i, _i, _i, _f] + [_vp] * 6
+        lib.qicref_gdn_create.restype = _vp
+        lib.qicref_gdn_run.argtypes = [_vp] * 6
+        lib.qicref_gdn_run.restype = _i
+        lib.qicref_gdn_states.argtypes = [_vp] * 3
+        lib.qicref_gdn_destroy.argtypes = [_vp]
         self.lib = lib
 
     @staticmethod
@@ -253,3 +259,42 @@ class RefGatedDelta:
         if rc != 0:
             raise RuntimeError("reference GatedDeltaNet step failed")
         return out, cs, rs
+
+    def layer(self, *, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, num_k_heads, num_v_heads,
+              k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6):
+        """One linear-attention layer of the reference model, set up once (weights on the
+        device, cuBLAS handle), for repeated steps; close() releases it."""
+        return _RefGatedDeltaLayer(self.lib, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state,
+                                   num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps)
+
+
+class _RefGatedDeltaLayer:
+    def __init__(self, lib, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, Hk, Hv, dk, dv, K, eps):
+        self.lib = lib
+        self.shapes = (Hk, Hv, dk, dv, K)
+        ws = [_cpu(t) for t in (conv_w, dt_bias, a_log, norm_w)]
+        if any(t.dtype != torch.float16 for t in ws):
+            raise TypeError("the reference's GatedDeltaNet step is fp16")
+        cs = _cpu(conv_state).float().contiguous()
+        rs = _cpu(recurrent_state).float().contiguous()
+        self.h = lib.qicref_gdn_create(Hk, Hv, dk, dv, K, eps, *[_p(t) for t in ws], _p(cs), _p(rs))
+        if not self.h:
+            raise RuntimeError("reference GatedDeltaNet set-up failed")
+
+    def run(self, qkv=None, z=None, b=None, a=None, out=None):
+        """One step; qkv/z/b/a (CPU fp16) replace the previous step's projections when given."""
+        ins = [None if t is None else _cpu(t) for t in (qkv, z, b, a)]
+        if self.lib.qicref_gdn_run(self.h, *[_p(t) for t in ins], _p(out)) != 0:
+            raise RuntimeError("reference GatedDeltaNet step failed")
+
+    def states(self):
+        Hk, Hv, dk, dv, K = self.shapes
+        cs = torch.empty((2 * Hk * dk + Hv * dv) * K, dtype=torch.float32)
+        rs = torch.empty(Hv * dk * dv, dtype=torch.float32)
+        self.lib.qicref_gdn_states(self.h, _p(cs), _p(rs))
+        return cs, rs
+
+    def close(self):
+        if self.h:
+            self.lib.qicref_gdn_destroy(self.h)
+            self.h = None

@@ -54,22 +54,38 @@ half* to_device(const void* src, size_t bytes) {
 
 }  // namespace
 
-// One decode step of the reference's linear-attention block on host fp16 inputs
-// (qkv [2*Hk*dk + Hv*dv], z [Hv*dv], b/a/dt_bias/a_log [Hv], conv_w [conv_dim*K],
-// norm_w [dv]); conv_state [conv_dim*K] and recurrent_state [Hv*dk*dv] (fp32, host)
-// are updated in place; out [Hv*dv] receives the fp16 gated-norm output. Returns 0,
-// or 1 after printing the reference's CUDA/cuBLAS error.
-extern "C" int qicref_gdn_step(int Hk, int Hv, int dk, int dv, int K, float eps, const void* qkv, const void* z,
-                               const void* b, const void* a, const void* conv_w, const void* dt_bias,
-                               const void* a_log, const void* norm_w, float* conv_state, float* recurrent_state,
-                               void* out) {
+// The reference model set up for one linear-attention layer: weights and runtime
+// buffers on the device, the LayerCache states on the host, the cuBLAS handle
+// created once, as the reference's load() does.
+struct RefGdn {
+  QwenMiniModel m;  // its destructor frees the runtime buffers and the cuBLAS handle
   QwenMiniModel::LayerWeights w;
-  int rc = 0;
+  QwenMiniModel::LayerCache cache;
+  size_t key_dim = 0, val_dim = 0, conv_dim = 0;
+  int Hv = 0, K = 0, dk = 0, dv = 0;
+  ~RefGdn() {
+    for (half* p : {w.linear_in_qkv, w.linear_in_z, w.linear_in_b, w.linear_in_a, w.linear_conv1d_w,
+                    w.linear_dt_bias, w.linear_a_log, w.linear_norm_w, w.linear_out_proj})
+      if (p != nullptr) cudaFree(p);
+  }
+};
+
+// Host fp16 weights (conv_w [conv_dim*K], dt_bias/a_log [Hv], norm_w [dv]) and fp32
+// initial states (conv_state [conv_dim*K], recurrent_state [Hv*dk*dv]). Returns a
+// handle, or null after printing the reference's CUDA/cuBLAS error.
+extern "C" void* qicref_gdn_create(int Hk, int Hv, int dk, int dv, int K, float eps, const void* conv_w,
+                                   const void* dt_bias, const void* a_log, const void* norm_w,
+                                   const float* conv_state, const float* recurrent_state) {
+  RefGdn* r = new RefGdn();
   try {
-    const size_t key_dim = static_cast<size_t>(Hk) * dk;
-    const size_t val_dim = static_cast<size_t>(Hv) * dv;
-    const size_t conv_dim = 2 * key_dim + val_dim;
-    QwenMiniModel m;  // its destructor frees the runtime buffers and the cuBLAS handle set below
+    r->key_dim = static_cast<size_t>(Hk) * dk;
+    r->val_dim = static_cast<size_t>(Hv) * dv;
+    r->conv_dim = 2 * r->key_dim + r->val_dim;
+    r->Hv = Hv;
+    r->K = K;
+    r->dk = dk;
+    r->dv = dv;
+    QwenMiniModel& m = r->m;
     m.cfg_.hidden_size = 1;
     m.cfg_.linear_num_key_heads = Hk;
     m.cfg_.linear_num_value_heads = Hv;
@@ -81,34 +97,74 @@ extern "C" int qicref_gdn_step(int Hk, int Hv, int dk, int dv, int K, float eps,
     const half one = __float2half(1.0f);
     m.x_norm_ = to_device(&one, sizeof(half));
     m.x_ = to_device(nullptr, sizeof(half));
-    m.linear_mixed_qkv_ = to_device(nullptr, conv_dim * sizeof(half));
-    m.linear_z_ = to_device(nullptr, val_dim * sizeof(half));
+    m.linear_mixed_qkv_ = to_device(nullptr, r->conv_dim * sizeof(half));
+    m.linear_z_ = to_device(nullptr, r->val_dim * sizeof(half));
     m.linear_b_ = to_device(nullptr, Hv * sizeof(half));
     m.linear_a_ = to_device(nullptr, Hv * sizeof(half));
-    m.linear_out_ = to_device(nullptr, val_dim * sizeof(half));
+    m.linear_out_ = to_device(nullptr, r->val_dim * sizeof(half));
+    QwenMiniModel::LayerWeights& w = r->w;
     w.is_linear = true;
-    w.linear_in_qkv = to_device(qkv, conv_dim * sizeof(half));
-    w.linear_in_z = to_device(z, val_dim * sizeof(half));
-    w.linear_in_b = to_device(b, Hv * sizeof(half));
-    w.linear_in_a = to_device(a, Hv * sizeof(half));
-    w.linear_conv1d_w = to_device(conv_w, conv_dim * K * sizeof(half));
+    w.linear_in_qkv = to_device(nullptr, r->conv_dim * sizeof(half));
+    w.linear_in_z = to_device(nullptr, r->val_dim * sizeof(half));
+    w.linear_in_b = to_device(nullptr, Hv * sizeof(half));
+    w.linear_in_a = to_device(nullptr, Hv * sizeof(half));
+    w.linear_conv1d_w = to_device(conv_w, r->conv_dim * K * sizeof(half));
     w.linear_dt_bias = to_device(dt_bias, Hv * sizeof(half));
     w.linear_a_log = to_device(a_log, Hv * sizeof(half));
     w.linear_norm_w = to_device(norm_w, dv * sizeof(half));
-    w.linear_out_proj = to_device(nullptr, val_dim * sizeof(half));
-    QwenMiniModel::LayerCache cache;
-    cache.linear_conv_state.assign(conv_state, conv_state + conv_dim * K);
-    cache.linear_recurrent_state.assign(recurrent_state, recurrent_state + Hv * static_cast<size_t>(dk) * dv);
-    m.run_linear_attention_block(w, cache);
-    CUDA_CHECK(cudaMemcpy(out, m.linear_out_, val_dim * sizeof(half), cudaMemcpyDeviceToHost));
-    std::memcpy(conv_state, cache.linear_conv_state.data(), conv_dim * K * sizeof(float));
-    std::memcpy(recurrent_state, cache.linear_recurrent_state.data(), Hv * static_cast<size_t>(dk) * dv * sizeof(float));
+    w.linear_out_proj = to_device(nullptr, r->val_dim * sizeof(half));
+    r->cache.linear_conv_state.assign(conv_state, conv_state + r->conv_dim * K);
+    r->cache.linear_recurrent_state.assign(recurrent_state, recurrent_state + Hv * static_cast<size_t>(dk) * dv);
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "reference GatedDeltaNet set-up failed: %s\n", e.what());
+    delete r;
+    return nullptr;
+  }
+  return r;
+}
+
+// One decode step of the reference's linear-attention block. qkv [conv_dim], z
+// [Hv*dv], b and a [Hv] (host fp16) become the step's projections (null: the previous
+// step's again); out [Hv*dv] (host fp16) receives the gated-norm output, or null.
+extern "C" int qicref_gdn_run(void* handle, const void* qkv, const void* z, const void* b, const void* a, void* out) {
+  RefGdn* r = static_cast<RefGdn*>(handle);
+  try {
+    if (qkv != nullptr) {
+      CUDA_CHECK(cudaMemcpy(r->w.linear_in_qkv, qkv, r->conv_dim * sizeof(half), cudaMemcpyHostToDevice));
+      CUDA_CHECK(cudaMemcpy(r->w.linear_in_z, z, r->val_dim * sizeof(half), cudaMemcpyHostToDevice));
+      CUDA_CHECK(cudaMemcpy(r->w.linear_in_b, b, r->Hv * sizeof(half), cudaMemcpyHostToDevice));
+      CUDA_CHECK(cudaMemcpy(r->w.linear_in_a, a, r->Hv * sizeof(half), cudaMemcpyHostToDevice));
+    }
+    r->m.run_linear_attention_block(r->w, r->cache);
+    if (out != nullptr)
+      CUDA_CHECK(cudaMemcpy(out, r->m.linear_out_, r->val_dim * sizeof(half), cudaMemcpyDeviceToHost));
   } catch (const std::exception& e) {
     std::fprintf(stderr, "reference GatedDeltaNet step failed: %s\n", e.what());
-    rc = 1;
+    return 1;
   }
-  for (half* p : {w.linear_in_qkv, w.linear_in_z, w.linear_in_b, w.linear_in_a, w.linear_conv1d_w, w.linear_dt_bias,
-                  w.linear_a_log, w.linear_norm_w, w.linear_out_proj})
-    if (p != nullptr) cudaFree(p);
+  return 0;
+}
+
+// Copies the current states out (host fp32).
+extern "C" void qicref_gdn_states(void* handle, float* conv_state, float* recurrent_state) {
+  const RefGdn* r = static_cast<const RefGdn*>(handle);
+  std::memcpy(conv_state, r->cache.linear_conv_state.data(), r->conv_dim * r->K * sizeof(float));
+  std::memcpy(recurrent_state, r->cache.linear_recurrent_state.data(),
+              r->Hv * static_cast<size_t>(r->dk) * r->dv * sizeof(float));
+}
+
+extern "C" void qicref_gdn_destroy(void* handle) { delete static_cast<RefGdn*>(handle); }
+
+// One step on fresh state: conv_state and recurrent_state (host fp32) are updated in
+// place; out receives the step's output. Returns 0, or 1 after printing the error.
+extern "C" int qicref_gdn_step(int Hk, int Hv, int dk, int dv, int K, float eps, const void* qkv, const void* z,
+                               const void* b, const void* a, const void* conv_w, const void* dt_bias,
+                               const void* a_log, const void* norm_w, float* conv_state, float* recurrent_state,
+                               void* out) {
+  void* h = qicref_gdn_create(Hk, Hv, dk, dv, K, eps, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state);
+  if (h == nullptr) return 1;
+  const int rc = qicref_gdn_run(h, qkv, z, b, a, out);
+  if (rc == 0) qicref_gdn_states(h, conv_state, recurrent_state);
+  qicref_gdn_destroy(h);
   return rc;
 }
