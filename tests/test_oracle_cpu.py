@@ -209,3 +209,25 @@ def test_oracle_against_reference_golden(oracle, path):
         assert torch.equal(rs, case["recurrent_state"])
     else:
         pytest.fail(f"unknown golden kind {kind}")
+
+
+def test_gdn_golden_inputs_regenerate_from_their_seeds():
+    """tests/golden/make_gdn_golden.py still produces the inputs stored in the
+    committed GatedDeltaNet fixtures (same cases, same seeds, same draws)."""
+    import sys
+
+    sys.path.insert(0, str(GOLDEN))
+    import make_gdn_golden as gen
+
+    files = sorted(GOLDEN.glob("gdn_ref_*.pt"))
+    assert len(files) == len(gen.CASES)
+    for path in files:
+        case = torch.load(path)
+        assert tuple(case["case"]) in [tuple(c) for c in gen.CASES]
+        want = gen.case_inputs(*case["case"])
+        got = case["inputs"]
+        for k in ("conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state"):
+            assert torch.equal(got[k], want[k]), (path.name, k)
+        for t, (a, b) in enumerate(zip(got["steps"], want["steps"])):
+            for k in a:
+                assert torch.equal(a[k], b[k]), (path.name, t, k)
