@@ -1,0 +1,93 @@
+"""CPU checks of the batched-decode planner (qic_batch_plan, host code): with an
+explicit CTA target it queries no device, so its plan can be checked here. Every
+(sequence, kv head) has its pipeline stages covered exactly once by items with
+consistent split indices; partial slots do not collide; items are ordered longest
+first; the workspace covers every slot; targets are respected where they can be."""
+import ctypes
+
+import pytest
+
+from qwenincuda_b200 import abi
+
+ITEM_FIELDS = ("b", "kvh", "split", "nsplit", "st_lo", "st_hi", "seq_len", "part_base")
+
+
+def _plan(lens, H, Hkv, d, target):
+    L = abi.lib()
+    arr = (ctypes.c_int32 * len(lens))(*lens)
+    items = ctypes.c_int(0)
+    wsb = ctypes.c_size_t(0)
+    rc = L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), len(lens), H, Hkv, d, target, None, 0,
+                          ctypes.byref(items), ctypes.byref(wsb))
+    assert rc == 0
+    buf = (ctypes.c_int32 * (8 * items.value))()
+    n = items.value
+    rc = L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), len(lens), H, Hkv, d, target,
+                          ctypes.cast(buf, ctypes.c_void_p), n, ctypes.byref(items), ctypes.byref(wsb))
+    assert rc == 0 and items.value == n
+    plan = [dict(zip(ITEM_FIELDS, buf[8 * i:8 * i + 8])) for i in range(n)]
+    return plan, int(wsb.value)
+
+
+def _tok(d):
+    return 16 if d > 128 else 32
+
+
+@pytest.mark.parametrize("lens,H,Hkv,d", [
+    ([1, 2, 33, 777, 2049, 3001], 32, 8, 128),
+    ([32769, 1025, 17, 4096, 4097], 16, 4, 256),
+    ([100] * 40, 16, 8, 64),
+    ([131073], 32, 8, 128),
+])
+@pytest.mark.parametrize("target", [1, 7, 64, 444, 5000])
+def test_plan_covers_every_stage_once(lens, H, Hkv, d, target):
+    plan, ws_bytes = _plan(lens, H, Hkv, d, target)
+    tok = _tok(d)
+    G = H // Hkv
+    pf = ((G * (d + 1)) + 3) & ~3
+    cover = {}
+    for it in plan:
+        key = (it["b"], it["kvh"])
+        assert 0 <= it["b"] < len(lens) and 0 <= it["kvh"] < Hkv
+        assert it["seq_len"] == lens[it["b"]]
+        assert 0 <= it["split"] < it["nsplit"]
+        assert 0 <= it["st_lo"] < it["st_hi"]
+        cover.setdefault(key, []).append(it)
+    assert len(cover) == len(lens) * Hkv
+    slots = set()
+    for (b, kvh), its in cover.items():
+        n_st = (lens[b] + tok - 1) // tok
+        its.sort(key=lambda x: x["split"])
+        assert [x["split"] for x in its] == list(range(len(its)))
+        assert all(x["nsplit"] == len(its) for x in its)
+        # contiguous ranges that partition [0, n_st)
+        assert its[0]["st_lo"] == 0 and its[-1]["st_hi"] == n_st
+        for a, c in zip(its, its[1:]):
+            assert a["st_hi"] == c["st_lo"]
+        if len(its) > 1:
+            for x in its:
+                slot = x["part_base"] + x["split"]
+                assert slot not in slots
+                slots.add(slot)
+    # the workspace holds the header, the counters and every partial slot
+    if slots:
+        assert ws_bytes >= 256 + 8192 * 4 + (max(slots) + 1) * pf * 4
+    # longest items first
+    lengths = [it["st_hi"] - it["st_lo"] for it in plan]
+    assert lengths == sorted(lengths, reverse=True)
+    # the target is met unless one item per (sequence, kv head) already exceeds it
+    assert len(plan) <= max(target, len(lens) * Hkv)
+
+
+def test_plan_rejects_bad_arguments():
+    L = abi.lib()
+    items = ctypes.c_int(0)
+    wsb = ctypes.c_size_t(0)
+    arr = (ctypes.c_int32 * 2)(5, 0)
+    assert L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), 2, 32, 8, 128, 8, None, 0, ctypes.byref(items),
+                            ctypes.byref(wsb)) == 1  # an empty sequence
+    arr = (ctypes.c_int32 * 1)(5)
+    assert L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), 1, 32, 8, 96, 8, None, 0, ctypes.byref(items),
+                            ctypes.byref(wsb)) == 2  # head_dim 96
+    assert L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), 1, 32, 6, 128, 8, None, 0, ctypes.byref(items),
+                            ctypes.byref(wsb)) == 1  # 32 % 6
