@@ -188,6 +188,13 @@ int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status);
  * and, with flags, the block src/model.cpp:633-652. */
 int qic_decode_attention(const qic_decode_args* args, qic_stream_t stream);
 
+/* The launch shape qic_decode_attention uses for these arguments: splits per kv head
+ * and CTAs per thread-block cluster (its own choice when num_splits / cluster_size
+ * are 0), or 0 and 0 when seq_len is 0 (nothing is launched). With QIC_DEVICE_SEQ_LEN
+ * the shape follows seq_len, the bound. Reads the device's occupancy for the kernel;
+ * touches no argument pointer and allocates nothing. */
+int qic_decode_launch_shape(const qic_decode_args* args, int* num_splits, int* cluster_size);
+
 /* Same computation as qic_decode_attention, for callers that cannot allocate device
  * memory: code written against the reference's kernels.cuh interface has no workspace
  * to pass, and a per-token decode loop (or a host that reserves all HBM for its own

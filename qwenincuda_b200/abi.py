@@ -183,6 +183,8 @@ SIGNATURES = {
     "qic_workspace_init": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp]),
     "qic_workspace_status": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int)]),
     "qic_decode_attention": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
+    "qic_decode_launch_shape": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(ctypes.c_int),
+                                               ctypes.POINTER(ctypes.c_int)]),
     "qic_gated_delta_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), _vp]),
     "qic_batch_plan": (
         ctypes.c_int,

@@ -261,6 +261,59 @@ int box_height(bool paged, int page_size, int tok, int* log2) {
 
 namespace {
 
+// Splits per kv head and CTAs per cluster of a single-sequence launch over n_stages
+// pipeline stages: the caller's choice, else one wave of resident 8-CTA clusters
+// (five sixths of it with QIC_PDL), fewer for shorter sequences.
+int launch_shape(const qic_decode_args* a, bool cp, int n_stages, int* n_splits_out, int* cluster_out) {
+  const int D = a->head_dim, Hkv = a->num_kv_heads;
+  int n_splits = a->num_splits, cluster = a->cluster_size;
+  if (cluster < 0 || cluster > qic::kMaxCluster) return QIC_ERROR_INVALID_VALUE;
+  if (cp) cluster = qic::kCpSlices;
+  if (n_splits <= 0) {
+    // As many CTAs as can be resident in one wave: clusters of 8 (measured best on B200),
+    // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
+    // With programmatic dependent launch (layers chained back to back) a sixth of the
+    // resident slots is left free, so the next launch's CTAs start their copies while
+    // this one merges its splits (measured on 36 chained S=8192 layers: 13.6 -> 12.8
+    // us per layer; 8 chained d=256 S=32769 layers: 31.3 -> 30.2 us).
+    const bool auto_cluster = cluster == 0;
+    if (cluster == 0) cluster = 8;
+    int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
+    if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
+    if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
+    int nclust = std::max(1, max_clusters / Hkv);
+    n_splits = cluster * nclust;
+    if (auto_cluster) {
+      // Shorter sequences: about 6 stages per CTA (8 at d=256; 12 at d=64, the same
+      // bytes as d=128, not swept), in multiples of 8 CTAs, and a single cluster per
+      // kv head up to 16 CTAs, so the merge needs no cross-cluster step. Measured on
+      // 8 chained layers: d=128 S=1025 10.0 -> 8.9 us, S=2049 10.5 -> 9.5, S=4097
+      // 12.0 -> 11.5; d=256 S=2049 14.0 -> 12.1, S=8193 16.7 -> 15.6.
+      const int per_split = D >= 256 ? 8 : (D >= 128 ? 6 : 12);
+      const int want = std::max(8, n_stages / per_split / 8 * 8);
+      if (want < n_splits) {
+        n_splits = want;
+        if (want <= qic::kMaxCluster) cluster = want;
+      }
+    }
+    if (n_splits > n_stages) {
+      nclust = std::max(1, n_stages / cluster);
+      if (n_stages < cluster) cluster = n_stages;
+      n_splits = cluster * nclust;
+    }
+  }
+  if (cluster == 0) cluster = std::min(n_splits, qic::kMaxCluster);
+  while (cluster > 1 && n_splits % cluster != 0) --cluster;
+  if (n_splits > qic::kMaxSplits) return QIC_ERROR_INVALID_VALUE;
+  if (a->workspace == nullptr) {
+    n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
+    cluster = n_splits;
+  }
+  *n_splits_out = n_splits;
+  *cluster_out = cluster;
+  return QIC_SUCCESS;
+}
+
 // Single-sequence decode attention; cp != nullptr adds the context-parallel exchange.
 int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_stream_t stream) {
   if (a == nullptr) return QIC_ERROR_INVALID_VALUE;
@@ -330,49 +383,9 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   if (rc != QIC_SUCCESS) return rc;
 
   const int n_stages = (S + tok - 1) / tok;
-  int n_splits = a->num_splits, cluster = a->cluster_size;
-  if (cluster < 0 || cluster > qic::kMaxCluster) return QIC_ERROR_INVALID_VALUE;
-  if (cp != nullptr) cluster = qic::kCpSlices;
-  if (n_splits <= 0) {
-    // As many CTAs as can be resident in one wave: clusters of 8 (measured best on B200),
-    // as many clusters per kv head as the GPU holds at once; fewer for short sequences.
-    // With programmatic dependent launch (layers chained back to back) a sixth of the
-    // resident slots is left free, so the next launch's CTAs start their copies while
-    // this one merges its splits (measured on 36 chained S=8192 layers: 13.6 -> 12.8
-    // us per layer; 8 chained d=256 S=32769 layers: 31.3 -> 30.2 us).
-    const bool auto_cluster = cluster == 0;
-    if (cluster == 0) cluster = 8;
-    int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
-    if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
-    if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
-    int nclust = std::max(1, max_clusters / Hkv);
-    n_splits = cluster * nclust;
-    if (auto_cluster) {
-      // Shorter sequences: about 6 stages per CTA (8 at d=256; 12 at d=64, the same
-      // bytes as d=128, not swept), in multiples of 8 CTAs, and a single cluster per
-      // kv head up to 16 CTAs, so the merge needs no cross-cluster step. Measured on
-      // 8 chained layers: d=128 S=1025 10.0 -> 8.9 us, S=2049 10.5 -> 9.5, S=4097
-      // 12.0 -> 11.5; d=256 S=2049 14.0 -> 12.1, S=8193 16.7 -> 15.6.
-      const int per_split = D >= 256 ? 8 : (D >= 128 ? 6 : 12);
-      const int want = std::max(8, n_stages / per_split / 8 * 8);
-      if (want < n_splits) {
-        n_splits = want;
-        if (want <= qic::kMaxCluster) cluster = want;
-      }
-    }
-    if (n_splits > n_stages) {
-      nclust = std::max(1, n_stages / cluster);
-      if (n_stages < cluster) cluster = n_stages;
-      n_splits = cluster * nclust;
-    }
-  }
-  if (cluster == 0) cluster = std::min(n_splits, qic::kMaxCluster);
-  while (cluster > 1 && n_splits % cluster != 0) --cluster;
-  if (n_splits > qic::kMaxSplits) return QIC_ERROR_INVALID_VALUE;
-  if (a->workspace == nullptr) {
-    n_splits = std::min(n_splits, qic::kMaxCluster);  // merged on chip only, no workspace needed
-    cluster = n_splits;
-  }
+  int n_splits = 0, cluster = 0;
+  rc = launch_shape(a, cp != nullptr, n_stages, &n_splits, &cluster);
+  if (rc != QIC_SUCCESS) return rc;
   if (cp != nullptr && (cluster != qic::kCpSlices || n_splits % qic::kCpSlices != 0)) return QIC_ERROR_NOT_SUPPORTED;
   const int n_clusters = n_splits / cluster;
   if (n_clusters > 1) {
@@ -425,6 +438,18 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
 
 int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   return decode_attention_impl(a, nullptr, stream);
+}
+
+int qic_decode_launch_shape(const qic_decode_args* a, int* num_splits, int* cluster_size) {
+  if (a == nullptr || num_splits == nullptr || cluster_size == nullptr) return QIC_ERROR_INVALID_VALUE;
+  const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim, S = a->seq_len;
+  if (!valid_dtype(a->dtype) || H <= 0 || Hkv <= 0 || H % Hkv != 0 || S < 0) return QIC_ERROR_INVALID_VALUE;
+  if (!supported_head_dim(D) || H / Hkv > qic::kMaxGroup) return QIC_ERROR_NOT_SUPPORTED;
+  *num_splits = 0;
+  *cluster_size = 0;
+  if (S == 0) return QIC_SUCCESS;  // no launch
+  const int tok = qic::stage_tokens(D);
+  return launch_shape(a, false, (S + tok - 1) / tok, num_splits, cluster_size);
 }
 
 int qic_cp_decode_attention(const qic_decode_args* a, const qic_cp_args* cp, qic_stream_t stream) {

@@ -165,6 +165,22 @@ def _flags(fuse_q, fuse_append, pdl, q_gate_interleaved=False):
             (QIC_PDL if pdl else 0) | (QIC_Q_GATE_INTERLEAVED if q_gate_interleaved else 0))
 
 
+def decode_launch_shape(*, num_heads, num_kv_heads, head_dim, seq_len, dtype=torch.bfloat16, pdl=False,
+                        workspace=True, num_splits=0, cluster_size=0):
+    """(splits per kv head, CTAs per cluster) that qic_decode_attention uses for this
+    shape. workspace: whether the call passes one (without it the splits are merged
+    on chip only, at most 16)."""
+    a = DecodeArgs()
+    a.dtype = QIC_DTYPE_BF16 if dtype == torch.bfloat16 else QIC_DTYPE_F16
+    a.num_heads, a.num_kv_heads, a.head_dim, a.seq_len = num_heads, num_kv_heads, head_dim, seq_len
+    a.flags = QIC_PDL if pdl else 0
+    a.workspace = 16 if workspace else None  # only its presence is read
+    a.num_splits, a.cluster_size = num_splits, cluster_size
+    n, c = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().qic_decode_launch_shape(ctypes.byref(a), ctypes.byref(n), ctypes.byref(c)), "qic_decode_launch_shape")
+    return n.value, c.value
+
+
 def decode_attention(stream=None, **kw):
     """Split-KV decode attention; see qic_decode_attention in include/qic.h."""
     a = decode_args(**kw)

@@ -1,8 +1,12 @@
-"""CPU checks of the batched-decode planner (qic_batch_plan, host code): with an
-explicit CTA target it queries no device, so its plan can be checked here. Every
-(sequence, kv head) has its pipeline stages covered exactly once by items with
-consistent split indices; partial slots do not collide; items are ordered longest
-first; the workspace covers every slot; targets are respected where they can be."""
+"""CPU checks of the host-side launch planning.
+
+* The batched-decode planner (qic_batch_plan): with an explicit CTA target it queries
+  no device. Every (sequence, kv head) has its pipeline stages covered exactly once by
+  items with consistent split indices; partial slots do not collide; items are ordered
+  longest first; the workspace covers every slot; targets are respected where they can
+  be.
+* The single-sequence launch shape (qic_decode_launch_shape): the split rule, checked
+  against the shapes a B200 runs (exact values with the no-device occupancy fallback)."""
 import ctypes
 
 import pytest
@@ -91,3 +95,45 @@ def test_plan_rejects_bad_arguments():
                             ctypes.byref(wsb)) == 2  # head_dim 96
     assert L.qic_batch_plan(ctypes.cast(arr, ctypes.c_void_p), 1, 32, 6, 128, 8, None, 0, ctypes.byref(items),
                             ctypes.byref(wsb)) == 1  # 32 % 6
+
+
+# (head_dim, H, Hkv, S, pdl) -> (splits per kv head, CTAs per cluster), for a GPU
+# holding three 128-thread CTAs per SM on 148 SMs (the host fallback when no device
+# answers the occupancy query; a B200 reports the same: grid (40, 8) at S=8192)
+SHAPES = {
+    (128, 32, 8, 1025, True): (8, 8), (128, 32, 8, 2049, True): (8, 8), (128, 32, 8, 3073, True): (16, 16),
+    (128, 32, 8, 4097, True): (16, 16), (128, 32, 8, 6145, True): (32, 8), (128, 32, 8, 8192, True): (40, 8),
+    (128, 32, 8, 8192, False): (40, 8), (128, 32, 8, 131073, True): (40, 8), (128, 32, 8, 131073, False): (48, 8),
+    (256, 16, 4, 2049, True): (16, 16), (256, 16, 4, 8193, True): (64, 8), (256, 16, 4, 32769, True): (88, 8),
+    (128, 32, 8, 100, False): (4, 4), (128, 16, 8, 1, False): (1, 1),
+}
+
+
+@pytest.mark.parametrize("key", list(SHAPES), ids=lambda k: "d{}_h{}_kv{}_s{}_{}".format(*k))
+def test_decode_launch_shape(key):
+    """qic_decode_launch_shape: one wave of resident 8-CTA clusters (five sixths with
+    QIC_PDL), about 6 (d=128) or 8 (d=256) stages per CTA below that, one cluster per
+    kv head up to 16 CTAs; never more splits than stages."""
+    import torch
+
+    import qwenincuda_b200 as q
+
+    d, H, Hkv, S, pdl = key
+    n, c = q.ops.decode_launch_shape(num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=S, pdl=pdl)
+    tok = _tok(d)
+    assert 1 <= c <= 16 and n % c == 0 and n <= max(1, (S + tok - 1) // tok)
+    if not torch.cuda.is_available():
+        assert (n, c) == SHAPES[key]
+
+
+def test_decode_launch_shape_explicit_and_without_workspace():
+    import qwenincuda_b200 as q
+
+    shape = lambda **kw: q.ops.decode_launch_shape(num_heads=32, num_kv_heads=8, head_dim=128, **kw)
+    assert shape(seq_len=8192, num_splits=24, cluster_size=8) == (24, 8)
+    assert shape(seq_len=8192, num_splits=24, cluster_size=0) == (24, 12)  # largest cluster <= 16 dividing 24
+    n, c = shape(seq_len=8192, workspace=False)
+    assert n == c and n <= 16  # merged on chip only
+    assert shape(seq_len=0) == (0, 0)
+    with pytest.raises(q.QicError):
+        shape(seq_len=100, cluster_size=17)
