@@ -281,7 +281,8 @@ int launch_shape(const qic_decode_args* a, bool cp, int n_stages, int* n_splits_
     int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
-    int nclust = std::max(1, max_clusters / Hkv);
+    // at most kMaxSplits splits per kv head: with one or two kv heads the wave is larger
+    int nclust = std::max(1, std::min(max_clusters / Hkv, qic::kMaxSplits / cluster));
     n_splits = cluster * nclust;
     if (auto_cluster) {
       // Shorter sequences: about 6 stages per CTA (8 at d=256; 12 at d=64, the same

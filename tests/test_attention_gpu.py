@@ -64,6 +64,13 @@ CASES = [
     (16, 8, 128, 129, 48),      # page size not a power of two (box height 16)
     (16, 8, 128, 300, 64),      # pages larger than a stage
     (4, 2, 256, 95, 24),        # box height 8
+    (24, 8, 128, 1000, 16),     # group 3
+    (40, 8, 128, 2000, 16),     # group 5
+    (48, 8, 64, 700, 32),       # group 6, head_dim 64
+    (28, 4, 256, 900, 16),      # group 7, head_dim 256
+    (8, 1, 128, 3000, 16),      # one kv head, group 8
+    (8, 1, 128, 40000, 16),     # one kv head, long: 208 splits, 26 clusters merged across
+    (2, 2, 256, 17, 8),         # group 1, head_dim 256
 ]
 
 

@@ -135,3 +135,25 @@ def test_batched_interleaved_q_gate_matches_split():
         outs.append((inp["out"].clone(), inp["k_cache"].clone()))
     assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
     assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+
+
+def test_batched_odd_group_vs_reference():
+    """Group 3 at head_dim 64: every sequence against the reference's paged kernel."""
+    cfg = _small_cfg(num_heads=24, num_kv_heads=8, head_dim=64, seed=15)
+    lens = [5, 300, 1000, 64]
+    inp = make_batched_inputs(cfg, seq_lens=lens)
+    plan = q.BatchPlan(lens, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
+    q.batch_decode_attention(plan=plan, q=inp["q"], k_cache=inp["k_cache"], v_cache=inp["v_cache"],
+                             block_tables=inp["block_tables"], out=inp["out"], num_heads=cfg.num_heads,
+                             num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, page_size=cfg.page_size)
+    torch.cuda.synchronize()
+    assert plan.status() == 0
+    ref = RefKernels(torch.bfloat16)
+    kc = inp["k_cache"].view(-1, cfg.kv_dim)
+    vc = inp["v_cache"].view(-1, cfg.kv_dim)
+    for b, S in enumerate(lens):
+        want = torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+        ref.paged_attention(inp["q"][b].flatten(), kc, vc, inp["block_tables"][b], cfg.page_size, cfg.num_heads,
+                            cfg.num_kv_heads, cfg.head_dim, S, want)
+        ok, err, idx = allclose_report(inp["out"][b], want, ATOL, RTOL)
+        assert ok, f"sequence {b} (S={S}): max err {err} at {idx}"

@@ -106,6 +106,8 @@ SHAPES = {
     (128, 32, 8, 8192, False): (40, 8), (128, 32, 8, 131073, True): (40, 8), (128, 32, 8, 131073, False): (48, 8),
     (256, 16, 4, 2049, True): (16, 16), (256, 16, 4, 8193, True): (64, 8), (256, 16, 4, 32769, True): (88, 8),
     (128, 32, 8, 100, False): (4, 4), (128, 16, 8, 1, False): (1, 1),
+    # one kv head: the wave (55 clusters of 8) exceeds the 256 splits a kv head may have
+    (128, 8, 1, 131073, False): (256, 8), (128, 8, 1, 131073, True): (256, 8), (128, 8, 1, 40000, False): (208, 8),
 }
 
 
