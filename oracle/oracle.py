@@ -7,10 +7,11 @@
   reference's own src/kernels.cu compiled unchanged for sm_100a (oracle/Makefile).
   Takes CUDA torch tensors; launches on the legacy default stream like the
   reference and synchronises.
-* ``RefGatedDelta``: ctypes binding of oracle/_ref/libqicref_gdn.so, the reference's
-  own GatedDeltaNet decode step (src/model.cpp:656-795, compiled unchanged inside
-  oracle/ref_gdn_harness.cpp). Takes and returns CPU tensors (fp16 inputs, fp32
-  states); needs a CUDA device, through which the reference copies its inputs.
+* ``RefGatedDelta``: ctypes binding of oracle/_ref/libqicref_gdn{,_bf16}.so, the
+  reference's own GatedDeltaNet decode step (src/model.cpp:656-795, compiled unchanged
+  inside oracle/ref_gdn_harness.cpp; fp16, or the bfloat16 instance). Takes and returns
+  CPU tensors (16-bit inputs, fp32 states); needs a CUDA device, through which the
+  reference copies its inputs.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs
 use this module; the product library never does.
@@ -224,10 +225,11 @@ class RefKernels:
 
 class RefGatedDelta:
     """The reference's own GatedDeltaNet decode step (run_linear_attention_block,
-    src/model.cpp:656-795), fp16 as the reference ships it."""
+    src/model.cpp:656-795): fp16 as the reference ships it, or its bfloat16 instance."""
 
-    def __init__(self):
-        path = REF_DIR / "libqicref_gdn.so"
+    def __init__(self, dtype: torch.dtype = torch.float16):
+        self.dtype = dtype
+        path = REF_DIR / ("libqicref_gdn.so" if dtype == torch.float16 else "libqicref_gdn_bf16.so")
         if not path.exists():
             raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
         lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
@@ -242,18 +244,18 @@ class RefGatedDelta:
         self.lib = lib
 
     @staticmethod
-    def available() -> bool:
-        return (REF_DIR / "libqicref_gdn.so").exists()
+    def available(dtype: torch.dtype = torch.float16) -> bool:
+        return (REF_DIR / ("libqicref_gdn.so" if dtype == torch.float16 else "libqicref_gdn_bf16.so")).exists()
 
     def step(self, *, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, num_k_heads,
              num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6):
         """Returns (out, new conv_state, new recurrent_state); inputs are not modified."""
         ins = [_cpu(t) for t in (qkv, z, b, a, conv_w, dt_bias, a_log, norm_w)]
-        if any(t.dtype != torch.float16 for t in ins):
-            raise TypeError("the reference's GatedDeltaNet step is fp16")
+        if any(t.dtype != self.dtype for t in ins):
+            raise TypeError(f"this instance of the reference's step takes {self.dtype}")
         cs = _cpu(conv_state).float().clone()
         rs = _cpu(recurrent_state).float().clone()
-        out = torch.empty(num_v_heads * v_head_dim, dtype=torch.float16)
+        out = torch.empty(num_v_heads * v_head_dim, dtype=self.dtype)
         rc = self.lib.qicref_gdn_step(num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps,
                                       *[_p(t) for t in ins], _p(cs), _p(rs), _p(out))
         if rc != 0:
@@ -264,17 +266,18 @@ class RefGatedDelta:
               k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6):
         """One linear-attention layer of the reference model, set up once (weights on the
         device, cuBLAS handle), for repeated steps; close() releases it."""
-        return _RefGatedDeltaLayer(self.lib, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state,
-                                   num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps)
+        return _RefGatedDeltaLayer(self.lib, self.dtype, conv_w, dt_bias, a_log, norm_w, conv_state,
+                                   recurrent_state, num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps)
 
 
 class _RefGatedDeltaLayer:
-    def __init__(self, lib, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, Hk, Hv, dk, dv, K, eps):
+    def __init__(self, lib, dtype, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, Hk, Hv, dk, dv, K,
+                 eps):
         self.lib = lib
         self.shapes = (Hk, Hv, dk, dv, K)
         ws = [_cpu(t) for t in (conv_w, dt_bias, a_log, norm_w)]
-        if any(t.dtype != torch.float16 for t in ws):
-            raise TypeError("the reference's GatedDeltaNet step is fp16")
+        if any(t.dtype != dtype for t in ws):
+            raise TypeError(f"this instance of the reference's step takes {dtype}")
         cs = _cpu(conv_state).float().contiguous()
         rs = _cpu(recurrent_state).float().contiguous()
         self.h = lib.qicref_gdn_create(Hk, Hv, dk, dv, K, eps, *[_p(t) for t in ws], _p(cs), _p(rs))

@@ -1,4 +1,5 @@
-// TEST INFRASTRUCTURE ONLY: runs the reference's own GatedDeltaNet decode step.
+// TEST INFRASTRUCTURE ONLY: runs the reference's own GatedDeltaNet decode step (fp16
+// as it ships, or a bfloat16 instance built with QICREF_GDN_BF16).
 //
 // The reference keeps this step in a private member, QwenMiniModel::
 // run_linear_attention_block (src/model.cpp:656-795 of the QweninCuda project): four
@@ -34,6 +35,17 @@
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
+
+#ifdef QICREF_GDN_BF16
+// bfloat16 instance: the reference's `half`, its two conversion calls and the cuBLAS
+// element type of its GEMV renamed to their bfloat16 counterparts, after every header
+// that defines them (the same renaming oracle/ref_bf16_shim.h applies to kernels.cu)
+#include <cuda_bf16.h>
+#define half __nv_bfloat16
+#define __half2float __bfloat162float
+#define __float2half __float2bfloat16
+#define CUDA_R_16F CUDA_R_16BF
+#endif
 
 #define private public
 #include "model.cpp"

@@ -65,23 +65,24 @@ def test_gdn_pdl_chain_matches_plain_launches(layers):
             assert torch.equal(x, y), f"layer {l} {name}"
 
 
-def test_gdn_kernel_vs_reference_step():
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gdn_kernel_vs_reference_step(dtype):
     """The CUDA kernel against the reference's own decode step (run_linear_attention_block,
-    src/model.cpp:656-795, run unchanged through oracle/_ref/libqicref_gdn.so) on fp16
-    inputs over three steps carrying the states: output within max-abs 2e-3 / rel 1e-2,
-    conv state exact, recurrent state within fp32 rounding."""
+    src/model.cpp:656-795, run unchanged through oracle/_ref: fp16 as shipped and its
+    bfloat16 instance) over three steps carrying the states: output within max-abs
+    2e-3 / rel 1e-2, conv state exact, recurrent state within fp32 rounding."""
     from oracle.oracle import RefGatedDelta
 
-    ref = RefGatedDelta()
+    ref = RefGatedDelta(dtype)
     Hk, Hv = 4, 8
     cfg = GdnConfig(num_k_heads=Hk, num_v_heads=Hv)
-    dev = make_gdn_inputs(cfg, device="cuda", dtype=torch.float16)
+    dev = make_gdn_inputs(cfg, device="cuda", dtype=dtype)
     host = {k: v.cpu().clone() for k, v in dev.items()}
     g = torch.Generator(device="cuda").manual_seed(78)
     for step in range(3):
         if step:
             for k, n in (("qkv", cfg.conv_dim), ("z", Hv * 128), ("b", Hv), ("a", Hv)):
-                new = torch.randn(n, generator=g, device="cuda").to(torch.float16)
+                new = torch.randn(n, generator=g, device="cuda").to(dtype)
                 dev[k].copy_(new)
                 host[k] = new.cpu()
         q.gated_delta_decode(**dev, num_k_heads=Hk, num_v_heads=Hv)
