@@ -99,6 +99,10 @@ enum {
                                     not with context parallelism. */
 };
 
+/* Longest sequence (tokens attended, and token positions) any entry point accepts:
+ * 2^30, beyond any cache that fits a GPU. Longer lengths return QIC_ERROR_INVALID_VALUE. */
+#define QIC_MAX_SEQ_LEN 1073741824
+
 const char* qic_status_string(int status);
 int qic_last_cuda_error(void);    /* cudaError_t of the last QIC_ERROR_CUDA on this thread */
 int qic_version(void);

@@ -156,7 +156,7 @@ int qic_kv_append(int dtype, const void* k_new, const void* v_new, const void* k
                   int position, void* k_cache, void* v_cache, const int32_t* page_table, int page_size,
                   int64_t cache_tokens, int num_kv_heads, int head_dim, qic_stream_t stream) {
   if (!valid_dtype(dtype) || !k_new || !v_new || !k_norm_w || !k_cache || !v_cache || num_kv_heads <= 0 ||
-      position < 0 || cache_tokens <= 0)
+      position < 0 || position >= QIC_MAX_SEQ_LEN || cache_tokens <= 0)
     return QIC_ERROR_INVALID_VALUE;
   if (!supported_head_dim(head_dim)) return QIC_ERROR_NOT_SUPPORTED;
   if (page_table != nullptr && page_size <= 0) return QIC_ERROR_INVALID_VALUE;
@@ -169,7 +169,8 @@ int qic_kv_append(int dtype, const void* k_new, const void* v_new, const void* k
 }
 
 size_t qic_decode_workspace_bytes(int num_heads, int num_kv_heads, int head_dim, int max_seq_len) {
-  if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_seq_len < 0) return 0;
+  if (num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_seq_len < 0 || max_seq_len > QIC_MAX_SEQ_LEN)
+    return 0;
   const int G = num_heads / num_kv_heads;
   const int tok = qic::stage_tokens(head_dim);
   const int n_stages = (max_seq_len + tok - 1) / tok;
@@ -322,7 +323,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   int rc = check_attention_common(a->dtype, H, Hkv, D, a->flags, a->q, a->out, a->k_cache, a->v_cache, a->gate,
                                   a->q_norm_w, a->k_norm_w, a->k_new, a->v_new, a->workspace);
   if (rc != QIC_SUCCESS) return rc;
-  if (S < 0) return QIC_ERROR_INVALID_VALUE;
+  if (S < 0 || S > QIC_MAX_SEQ_LEN) return QIC_ERROR_INVALID_VALUE;
   // device-resident length: seq_len is its upper bound and sizes the launch
   const bool dev_len = (a->flags & QIC_DEVICE_SEQ_LEN) != 0;
   if (dev_len && (a->seq_len_dev == nullptr || (reinterpret_cast<uintptr_t>(a->seq_len_dev) & 3u) != 0 || S < 1 ||
@@ -346,7 +347,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool partial_out = (a->flags & QIC_PARTIAL_OUT) != 0;
   if (partial_out && (cp != nullptr || !aligned16(a->out))) return QIC_ERROR_INVALID_VALUE;
-  if ((a->flags & QIC_EXPLICIT_POSITION) && (a->position < 0 || a->position > INT32_MAX - 1))
+  if ((a->flags & QIC_EXPLICIT_POSITION) && (a->position < 0 || a->position >= QIC_MAX_SEQ_LEN))
     return QIC_ERROR_INVALID_VALUE;
   if (cp != nullptr) {
     if (cp->world < 1 || cp->world > qic::kMaxRanks || cp->rank < 0 || cp->rank >= cp->world ||
@@ -444,7 +445,8 @@ int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
 int qic_decode_launch_shape(const qic_decode_args* a, int* num_splits, int* cluster_size) {
   if (a == nullptr || num_splits == nullptr || cluster_size == nullptr) return QIC_ERROR_INVALID_VALUE;
   const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim, S = a->seq_len;
-  if (!valid_dtype(a->dtype) || H <= 0 || Hkv <= 0 || H % Hkv != 0 || S < 0) return QIC_ERROR_INVALID_VALUE;
+  if (!valid_dtype(a->dtype) || H <= 0 || Hkv <= 0 || H % Hkv != 0 || S < 0 || S > QIC_MAX_SEQ_LEN)
+    return QIC_ERROR_INVALID_VALUE;
   if (!supported_head_dim(D) || H / Hkv > qic::kMaxGroup) return QIC_ERROR_NOT_SUPPORTED;
   *num_splits = 0;
   *cluster_size = 0;
@@ -531,7 +533,7 @@ int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv
   const int tok = qic::stage_tokens(head_dim);
   long long total = 0;
   for (int b = 0; b < batch; ++b) {
-    if (seq_lens[b] < 1) return QIC_ERROR_INVALID_VALUE;
+    if (seq_lens[b] < 1 || seq_lens[b] > QIC_MAX_SEQ_LEN) return QIC_ERROR_INVALID_VALUE;
     total += static_cast<long long>((seq_lens[b] + tok - 1) / tok) * num_kv_heads;
   }
   if (target_ctas <= 0) {
