@@ -205,15 +205,22 @@ int qic_decode_launch_shape(const qic_decode_args* args, int* num_splits, int* c
  * page pool) must not call cudaMalloc, which synchronises the device. The split-KV
  * scratch is a 2 MiB array inside this library (qic_noalloc_scratch_bytes), held by
  * every GPU that loads it until the process exits; args->workspace and
- * args->workspace_bytes are ignored. The first call on a device looks up the array's
- * address (make it before any stream capture). Each call clears the array's status
- * word and counters; calls that overlap on the GPU share the array and race. Shapes
- * whose partials do not fit return QIC_ERROR_WORKSPACE. No counterpart in the
+ * args->workspace_bytes are ignored. The first call on a device (and again after a
+ * cudaDeviceReset) looks up the array's address: make it before any stream capture.
+ * Each call clears the array's merge counters; calls that overlap on the GPU share
+ * the array and race. The array's device status word (QIC_DEV_* bits: bad page, bad
+ * device length, timeout) accumulates over calls until qic_noalloc_status reads it.
+ * Shapes whose partials do not fit return QIC_ERROR_WORKSPACE. No counterpart in the
  * reference: its kernels keep no scratch. Allocates nothing. */
 int qic_decode_attention_noalloc(const qic_decode_args* args, qic_stream_t stream);
 
 /* Size in bytes of the array qic_decode_attention_noalloc uses. */
 size_t qic_noalloc_scratch_bytes(void);
+
+/* Reads and clears the device status word of the current device's
+ * qic_decode_attention_noalloc array (QIC_DEV_* bits of every call since the last
+ * read); synchronises `stream`. No counterpart in the reference. */
+int qic_noalloc_status(qic_stream_t stream, int* dev_status);
 
 /* Floats per kv head of a QIC_PARTIAL_OUT partial: ((H/Hkv)*(d+1)+3) & ~3. */
 size_t qic_partial_floats(int num_heads, int num_kv_heads, int head_dim);

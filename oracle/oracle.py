@@ -147,7 +147,7 @@ class RefKernels:
         name = "libqicref_bf16.so" if dtype == torch.bfloat16 else "libqicref_f16.so"
         path = REF_DIR / name
         if not path.exists():
-            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref REF=<reference project root>)")
         lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
         lib.qicref_head_rmsnorm.argtypes = [_vp, _vp, _i, _i, _f, _vp]
         lib.qicref_rope_inplace.argtypes = [_vp, _i, _i, _i, _f]
@@ -231,7 +231,7 @@ class RefGatedDelta:
         self.dtype = dtype
         path = REF_DIR / ("libqicref_gdn.so" if dtype == torch.float16 else "libqicref_gdn_bf16.so")
         if not path.exists():
-            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref REF=<reference project root>)")
         lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
         lib.qicref_gdn_step.argtypes = [_i, _i, _i, _i, _i, _f] + [_vp] * 11
         lib.qicref_gdn_step.restype = _i

@@ -195,6 +195,7 @@ SIGNATURES = {
     "qic_batch_decode_attention": (ctypes.c_int, [ctypes.POINTER(BatchDecodeArgs), _vp]),
     "qic_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
     "qic_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "qic_noalloc_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "qic_partial_floats": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qic_attention_merge": (
         ctypes.c_int, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),

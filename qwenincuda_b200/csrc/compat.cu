@@ -3,8 +3,11 @@
 //
 // The hot-path shims forward to the C-ABI on the legacy default stream. The
 // attention shims own one split-KV workspace per device, allocated (and zeroed) on
-// first use and grown when a larger shape needs it. Failures are kept in a sticky
-// status (qic_compat_last_status) because the reference's functions return void.
+// the first attention call with room for the shape's largest split count at any
+// length, so a decode loop whose length grows token by token never allocates again;
+// only a later call with a larger head shape replaces it (once). Failures are kept in
+// a sticky status (qic_compat_last_status) because the reference's functions return
+// void.
 //
 // The five remaining kernels.cuh entries (embedding lookup, RMSNorm, q/gate split,
 // residual add, SwiGLU) are plain elementwise kernels provided so the surface is
@@ -36,7 +39,9 @@ struct DeviceWorkspace {
 std::mutex g_ws_mutex;
 DeviceWorkspace g_ws[64];
 
-// Returns a zeroed workspace of at least `need` bytes for the current device.
+// Returns a zeroed workspace of at least `need` bytes for the current device. The
+// callers ask for the bytes of the shape at QIC_MAX_SEQ_LEN (the split count is capped
+// there), so the size does not grow with the sequence.
 void* compat_workspace(size_t need, size_t* have) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
@@ -78,7 +83,7 @@ void attention_shim(const half* q, const half* k_cache, const half* v_cache, con
   a.page_table = page_table;
   a.out = context;
   if (num_heads > 0 && num_kv_heads > 0) {
-    const size_t need = qic_decode_workspace_bytes(num_heads, num_kv_heads, head_dim, seq_len);
+    const size_t need = qic_decode_workspace_bytes(num_heads, num_kv_heads, head_dim, QIC_MAX_SEQ_LEN);
     size_t have = 0;
     a.workspace = compat_workspace(need, &have);
     a.workspace_bytes = have;

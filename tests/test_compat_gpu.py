@@ -93,3 +93,35 @@ def test_compat_norm_rope_gate_match_reference():
     torch.cuda.synchronize()
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
     assert L.qic_compat_last_status() == 0
+
+
+def test_compat_decode_loop_allocates_once():
+    """A decode loop through launch_paged_attention whose length grows from 1 to 8192
+    tokens (the reference's decode_next, src/model.cpp:643-650) takes the shim's
+    workspace on its first call and no device memory after it; the last call matches
+    the reference's paged kernel."""
+    fns, L = _compat()
+    H, Hkv, d, P, S_max = 32, 8, 128, 16, 8192
+    g = torch.Generator(device="cuda").manual_seed(5)
+    npages = S_max // P
+    qv = torch.randn(H * d, generator=g, device="cuda").half()
+    kc = (torch.randn(npages * P, Hkv * d, generator=g, device="cuda") * 0.5).half()
+    vc = (torch.randn(npages * P, Hkv * d, generator=g, device="cuda") * 0.5).half()
+    table = torch.randperm(npages, generator=g, device="cuda").to(torch.int32)
+    got = torch.empty(H * d, device="cuda", dtype=torch.float16)
+
+    def call(S):
+        fns["paged"](qv.data_ptr(), kc.data_ptr(), vc.data_ptr(), table.data_ptr(), P, H, Hkv, d, S, got.data_ptr())
+
+    call(1)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for S in list(range(2, 300)) + list(range(300, S_max, 61)) + [S_max]:
+        call(S)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert L.qic_compat_last_status() == 0
+    want = torch.empty_like(got)
+    RefKernels(torch.float16).paged_attention(qv, kc, vc, table, P, H, Hkv, d, S_max, want)
+    ok, err, idx = allclose_report(got, want, ATOL, RTOL)
+    assert ok, f"max err {err} at {idx}"

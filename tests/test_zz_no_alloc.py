@@ -3,8 +3,11 @@ device memory (code written against the reference's kernels.cuh interface has no
 workspace to pass, and a per-token decode loop must not stop for a synchronising
 cudaMalloc). Its scratch is a fixed array inside the library; this checks, through
 the C-ABI, that two calls in a row give the same results as qic_decode_attention
-with a caller-allocated workspace. Collected last so a failure here comes after
-every other test has run; it also passes alone in a fresh process."""
+with a caller-allocated workspace, that repeated calls take no device memory, and
+that the array's device status word reports a bad page-table entry to
+qic_noalloc_status instead of being cleared by the next call. Collected last so a
+failure here comes after every other test has run; it also passes alone in a fresh
+process."""
 import ctypes
 
 import pytest
@@ -18,11 +21,18 @@ pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-3, 1e-2
 
 
-def _args(inp, layer, out, cfg, workspace=None):
+def _args(inp, layer, out, cfg, workspace=None, page_table=None):
     return q.ops.decode_args(
         q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=out, num_heads=cfg.num_heads,
-        num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len, page_table=inp.page_table[layer],
-        page_size=cfg.page_size, workspace=workspace, cache_tokens=inp.cache_tokens)
+        num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
+        page_table=inp.page_table[layer] if page_table is None else page_table, page_size=cfg.page_size,
+        workspace=workspace, cache_tokens=inp.cache_tokens)
+
+
+def _noalloc_status(L, stream):
+    v = ctypes.c_int(-1)
+    assert L.qic_noalloc_status(stream, ctypes.byref(v)) == 0
+    return v.value
 
 
 def test_noalloc_two_calls_match_workspace_entry_point():
@@ -42,8 +52,47 @@ def test_noalloc_two_calls_match_workspace_entry_point():
         assert L.qic_decode_attention_noalloc(ctypes.byref(b), stream) == 0
         torch.cuda.synchronize()
         assert ws.status() == 0
+        assert _noalloc_status(L, stream) == 0
         ok, err, idx = allclose_report(got, want, ATOL, RTOL)
         assert ok, f"call {layer}: max abs err {err} at {idx}"
+
+
+def test_noalloc_takes_no_device_memory():
+    """After the first call, repeated calls leave the device's free memory unchanged."""
+    L = q.lib()
+    cfg = AttnConfig("noalloc_mem", 32, 8, 128, 9000, layers=1, seed=23)
+    inp = make_attention_inputs(cfg, paged=True)
+    out = torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    a = _args(inp, 0, out, cfg)
+    assert L.qic_decode_attention_noalloc(ctypes.byref(a), stream) == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(20):
+        assert L.qic_decode_attention_noalloc(ctypes.byref(a), stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert _noalloc_status(L, stream) == 0
+
+
+def test_noalloc_reports_a_bad_page_entry():
+    """A page-table entry outside the cache is clamped by the kernel's bounds check and
+    its bit stays in the array's status word, through a later clean call, until
+    qic_noalloc_status reads (and clears) it."""
+    L = q.lib()
+    cfg = AttnConfig("noalloc_bad", 16, 8, 128, 256, layers=1, seed=24)
+    inp = make_attention_inputs(cfg, paged=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    bad = inp.page_table[0].clone()
+    bad[3] = 10 ** 6
+    out = torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+    assert _noalloc_status(L, stream) == 0
+    a = _args(inp, 0, out, cfg, page_table=bad)
+    assert L.qic_decode_attention_noalloc(ctypes.byref(a), stream) == 0
+    b = _args(inp, 0, out, cfg)  # a clean call after it keeps the bit
+    assert L.qic_decode_attention_noalloc(ctypes.byref(b), stream) == 0
+    assert _noalloc_status(L, stream) & q.abi.QIC_DEV_BAD_PAGE
+    assert _noalloc_status(L, stream) == 0  # cleared by the read
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
