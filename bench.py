@@ -13,12 +13,19 @@ metric: decode-attn KV-read GB/s = (K+V bytes read for S tokens + append bytes) 
 layer x layers / step time; also reported as us per layer. N > 1 GPUs (torchrun, one
 process per GPU): the default workload runs one independent replica per GPU (a
 single-sequence layer does not shard; weak scaling, value = N x bytes / the slowest
-rank's step time), and the same JSON line carries the partitioned configurations at
-that N: the 131073-token sequence split across the ranks with the fused in-kernel
-NVLink exchange (and the NCCL all-gather path timed beside it), and the 64-sequence
-batch partitioned by K/V bytes (strong scaling: total bytes / the slowest rank's
-time). --workload qwen3_8b_s131073 or qwen3_8b_batch64 with N > 1 makes those the
-line's value.
+rank's step time). At every N (N = 1 included) the same JSON line carries the
+partitioned configurations: `context_parallel_qwen3_8b_s131073` (the 131073-token
+sequence split across the ranks with the fused in-kernel NVLink exchange; the NCCL
+all-gather path timed beside it) and `partitioned_qwen3_8b_batch64` (the 64-sequence
+batch partitioned by K/V bytes), each with whole-job GB/s (total bytes / the slowest
+rank's time), the whole job timed on one GPU in the same run (rank 0 alone), the
+speed-up over it and the efficiency (speed-up / N). At N = 1 the line also carries
+`qwen35_gated_s32769`, `qwen3_0p6b_s1025` and `qwen35_gdn` (each with its roofline
+fraction) and `e2e_eager` (the end-to-end step without a CUDA graph: one C-ABI call
+per layer, with the host's time per call). --workload qwen3_8b_s131073 or
+qwen3_8b_batch64 with N > 1 makes a partitioned configuration the line's value.
+`config` is the same in this line and the reference arm's; run-dependent details
+are under `details`.
 
 Other workloads (--workload): qwen3_0p6b_s1025 (32 chained layers of S=1025, each with
 its own cache: 134 MB per step), qwen35_gated_s32769 (d=256;
@@ -431,7 +438,7 @@ def cp_workload(world, rank, with_allgather=True, layers=2):
     outs, out_views = _pack([torch.zeros(H * d, device="cuda", dtype=dtype) for _ in range(layers)])
     ws = q.Workspace(H, Hkv, d, n)  # the layers' calls are in stream order: one workspace, one exchange group
     owner = rank == world - 1
-    group = cpm.ExchangeGroup(H, Hkv, d, rank, world)
+    group = cpm.ExchangeGroup(H, Hkv, d, rank, world, gather=(lambda b, r, n: [b]) if world == 1 else None)
     kws = [dict(q=ins[3 * l], k_cache=kcs[l], v_cache=vcs[l], num_heads=H, num_kv_heads=Hkv, head_dim=d, seq_len=n,
                 page_table=tables[l], page_size=P, q_norm_w=ones, k_norm_w=ones, k_new=ins[3 * l + 1],
                 v_new=ins[3 * l + 2], eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True, fuse_append=owner,
@@ -482,7 +489,7 @@ def cp_workload(world, rank, with_allgather=True, layers=2):
                 keep=(kcs, vcs, tables, ins, outs, ws, group, args, packed),
                 config={"seq_len": S, "layers": layers, "page_size": P, "num_heads": H, "num_kv_heads": Hkv,
                         "head_dim": d, "ranks": world, "shard_tokens_rank0": cpm.shard_tokens(S, P, world)[0][1],
-                        "exchange": "in-kernel NVLink stores + system-scope flags, log-sum-exp merge"})
+                        "exchange": "in-kernel NVLink stores of tagged words, log-sum-exp merge"})
 
 
 def time_eager(fn, steps, warmup, world):
@@ -724,6 +731,47 @@ def reference_gpu(cfg, layers, steps, warmup):
             "build": "src/kernels.cu unmodified, nvcc -gencode arch=compute_100a,code=sm_100a --use_fast_math, bf16"}
 
 
+def line_config(workload, world):
+    """The JSON line's `config`: what the workload is, identical in both arms (this
+    library's and the reference's) for the same workload and N. Details that depend on
+    the run (plan items, per-rank shares) go under the line's `details` key instead."""
+    from qwenincuda_b200.workloads import CONFIGS, BatchConfig, GdnConfig, batched_bytes
+
+    if workload in ATTN_WORKLOADS:
+        cfg = CONFIGS[workload]
+        cp = workload == "qwen3_8b_s131073" and world > 1
+        layers = 2 if cp else cfg.layers
+        c = {"layout": "paged", "page_size": cfg.page_size, "layers": layers, "seq_len": cfg.seq_len,
+             "num_heads": cfg.num_heads, "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+             "gate": "interleaved q/gate projection" if cfg.gate else False}
+        rank_bytes = (cfg.kv_read_bytes() + cfg.append_bytes()) * layers // (world if cp else 1)
+        par = f"context-parallel{world}" if cp else (f"replicas{world}" if world > 1 else "single")
+    elif workload == "qwen35_gdn":
+        g = GdnConfig()
+        c = {"layers": GDN_STACK_LAYERS, "num_k_heads": g.num_k_heads, "num_v_heads": g.num_v_heads,
+             "k_head_dim": g.k_head_dim, "v_head_dim": g.v_head_dim, "conv_dim": g.conv_dim,
+             "conv_kernel": g.conv_kernel, "state": "fp32, resident on the device, one per layer"}
+        rank_bytes = g.state_bytes() * GDN_STACK_LAYERS
+        par = f"replicas{world}" if world > 1 else "single"
+    elif workload == "qwen35_pair":
+        att = CONFIGS["qwen35_gated_s32769"]
+        c = {"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)"}
+        rank_bytes = GdnConfig().state_bytes() + att.kv_read_bytes() + att.append_bytes()
+        par = f"replicas{world}" if world > 1 else "single"
+    elif workload == "qwen3_8b_batch64":
+        b = BatchConfig()
+        c = {"batch": b.batch, "seq_lens": f"U[{b.min_len},{b.max_len}]+1, seed {b.seed}", "page_size": b.page_size,
+             "pool_tokens": b.pool_tokens, "num_heads": b.num_heads, "num_kv_heads": b.num_kv_heads,
+             "head_dim": b.head_dim}
+        rank_bytes = batched_bytes(b.seq_lens(), b.kv_dim) // world
+        par = f"partitioned{world}" if world > 1 else "single"
+    else:
+        raise SystemExit(f"unknown workload {workload}")
+    l2 = ("step inputs larger than the 126 MB L2" if rank_bytes > (126 << 20)
+          else "step smaller than L2; consecutive steps re-read it")
+    return {"workload": workload, "parallelism": par, "l2": l2, **c}
+
+
 def run_reference_arm(args, world, rank):
     """The reference's own implementation of the path on this host's cores, on the
     same workload, metric and unit as this library's line (rank 0 only). For the
@@ -734,30 +782,21 @@ def run_reference_arm(args, world, rank):
     if rank != 0:
         return
     name = args.workload
+    config = line_config(name, world)
     cb = cpu_baseline(name, budget_s=max(2.0, min(20.0, 0.5 * args.steps)))
     layers = 1
     if name in ATTN_WORKLOADS:
         cfg = CONFIGS[name]
-        layers = cfg.layers
-        config = {"layout": "paged", "layers": layers, "seq_len": cfg.seq_len, "num_heads": cfg.num_heads,
-                  "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim, "gate": cfg.gate}
+        layers = config["layers"]
         step_bytes = (cfg.kv_read_bytes() + cfg.append_bytes()) * layers
     elif name == "qwen35_gdn":
-        g = GdnConfig()
         layers = GDN_STACK_LAYERS
-        config = {"layers": layers, "num_k_heads": g.num_k_heads, "num_v_heads": g.num_v_heads,
-                  "k_head_dim": g.k_head_dim, "v_head_dim": g.v_head_dim, "conv_dim": g.conv_dim,
-                  "conv_kernel": g.conv_kernel}
-        step_bytes = g.state_bytes() * layers
+        step_bytes = GdnConfig().state_bytes() * layers
     elif name == "qwen35_pair":
         att = CONFIGS["qwen35_gated_s32769"]
-        config = {"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)"}
         step_bytes = GdnConfig().state_bytes() + att.kv_read_bytes() + att.append_bytes()
     else:
         b = BatchConfig()
-        config = {"batch": b.batch, "seq_lens": f"U[{b.min_len},{b.max_len}]+1, seed {b.seed}",
-                  "page_size": b.page_size, "num_heads": b.num_heads, "num_kv_heads": b.num_kv_heads,
-                  "head_dim": b.head_dim}
         step_bytes = batched_bytes(b.seq_lens(), b.kv_dim)
     # the whole step of the workload at the sample's rate
     ms_step = step_bytes / (cb["value"] * 1e9) * 1e3
@@ -766,8 +805,9 @@ def run_reference_arm(args, world, rank):
         "metric": "GatedDeltaNet state GB/s" if name == "qwen35_gdn" else "decode-attn KV-read GB/s",
         "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 3), "us_per_layer": round(ms_step * 1000 / layers, 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": name, "parallelism": "single", **config},
+        "higher_is_better": True, "scaling": "strong" if world > 1 and name in ("qwen3_8b_s131073", "qwen3_8b_batch64") else "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config,
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -780,6 +820,70 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def summarize(wl, ms, ms_e2e, peaks, kernel_ms=None):
+    """One workload's figures on one GPU: GB/s, us per layer, the roofline fraction of
+    its dominant kernel, and the end-to-end figure."""
+    per_launch_ms = ms / wl["launches"]
+    achieved = wl["bytes_per_launch"] / ((kernel_ms if kernel_ms is not None else per_launch_ms) * 1e-3) / 1e9
+    return {"value": round(wl["bytes"] / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "us_per_layer": round(per_launch_ms * 1000, 3),
+            "roofline": {"bound": "hbm", "kernel": wl["kernel"], "achieved": round(achieved, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"]},
+            "e2e": {"value": round(wl["bytes"] / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2]},
+            "config": wl["config"]}
+
+
+def eager_e2e(wl, args):
+    """The workload's end-to-end step without a CUDA graph: the host-to-device copy of
+    the step's inputs from pinned memory, one C-ABI call per layer as a caller's decode
+    loop makes them (argument checks, TMA descriptors and the launch on the host, every
+    call), and the device-to-host copy of the outputs; timed with CUDA events. Also the
+    host time to issue one call (the loop runs ahead of the GPU)."""
+    fn = wl["e2e"][0]
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    host_s = time.perf_counter() - t0
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    return {"value": round(wl["bytes"] / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2],
+            "host_us_per_call": round(host_s * 1e6 / (args.steps * wl["launches"]), 2),
+            "what": "eager: pinned H2D copy, one qic_decode_attention call per layer, D2H copy; no CUDA graph"}
+
+
+def strong_scaling_key(make, args, world, rank, local, peaks):
+    """A partitioned configuration at this N (every rank its share, whole-job bytes /
+    the slowest rank's time) and, measured in the same run with rank 0 alone, the whole
+    job on one GPU: the speed-up over one GPU and the efficiency (speed-up / N)."""
+    ms1 = None
+    if world > 1:
+        if rank == 0:
+            wl1 = make(1, 0, False)
+            ms1, _, _ = measure(wl1, args, 1, local)
+            del wl1
+            torch.cuda.empty_cache()
+        barrier(world)
+    wl = make(world, rank, True)
+    res, ms, _, _ = partitioned_summary(wl, args, world, local, peaks)
+    del wl
+    torch.cuda.empty_cache()
+    if ms1 is None:
+        ms1 = ms
+    res["n1_us_per_step"] = round(ms1 * 1000, 2)
+    res["speedup_vs_n1"] = round(ms1 / ms, 3)
+    res["efficiency"] = round(ms1 / ms / world, 3)
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -789,6 +893,7 @@ def main():
     ap.add_argument("--workload", default="qwen3_8b_s8192")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="only the requested workload (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
@@ -811,11 +916,14 @@ def main():
     elif args.workload in ATTN_WORKLOADS:
         wl = attention_workload(args.workload, "paged", args.layers)
         ms, ms_e2e, clocks = measure(wl, args, world, local)
-        wl_c = attention_workload(args.workload, "contiguous", args.layers)
-        ms_c, _, _ = measure(wl_c, args, world, local)
-        extra["contiguous"] = {"value": round(world * wl_c["bytes"] / (ms_c * 1e-3) / 1e9, 2), "unit": "GB/s",
-                               "us_per_layer": round(ms_c / wl_c["launches"] * 1000, 3)}
-        del wl_c
+        if world == 1 and not args.no_extra:
+            extra["e2e_eager"] = eager_e2e(wl, args)
+        if not args.no_extra:
+            wl_c = attention_workload(args.workload, "contiguous", args.layers)
+            ms_c, _, _ = measure(wl_c, args, world, local)
+            extra["contiguous"] = {"value": round(world * wl_c["bytes"] / (ms_c * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                   "us_per_layer": round(ms_c / wl_c["launches"] * 1000, 3)}
+            del wl_c
     elif args.workload == "qwen35_gdn":
         wl = gdn_workload()
         ms, ms_e2e, clocks = measure(wl, args, world, local)
@@ -838,45 +946,56 @@ def main():
         # every rank processed its own share: whole-job bytes / the slowest rank's time
         total_bytes = sum_over_ranks(float(step_bytes), world)
         scaling = "strong"
-        parallelism = (f"context-parallel{world}" if args.workload == "qwen3_8b_s131073"
-                       else f"partitioned{world}")
     else:
         total_bytes = float(world * step_bytes)
         scaling = "weak"
-        parallelism = f"replicas{world}" if world > 1 else "single"
     value = total_bytes / (ms * 1e-3) / 1e9
     per_launch_ms = ms / wl["launches"]
     achieved = wl["bytes_per_launch"] / ((kernel_ms if kernel_ms is not None else per_launch_ms) * 1e-3) / 1e9
     traffic = measured_traffic(args.workload) if world == 1 else None
-    if world > 1 and args.workload == "qwen3_8b_s8192":
-        # the partitioned configurations at the same N (one JSON line per run)
-        wl_cp = cp_workload(world, rank)
-        extra["context_parallel_qwen3_8b_s131073"] = partitioned_summary(wl_cp, args, world, local, peaks)[0]
-        del wl_cp
-        wl_b = batched_workload(world, rank)
-        extra["partitioned_qwen3_8b_batch64"] = partitioned_summary(wl_b, args, world, local, peaks)[0]
-        del wl_b
+    details = wl["config"]
+    h2d, d2h, kernel_name, launches, bpl = wl["e2e"][1], wl["e2e"][2], wl["kernel"], wl["launches"], wl["bytes_per_launch"]
+    del wl
+    torch.cuda.empty_cache()
+    if args.workload == "qwen3_8b_s8192" and not args.no_extra:
+        # the partitioned configurations at this N (N = 1 included), each with its own
+        # one-GPU baseline, speed-up and efficiency
+        extra["context_parallel_qwen3_8b_s131073"] = strong_scaling_key(
+            lambda w, r, ag: cp_workload(w, r, with_allgather=ag), args, world, rank, local, peaks)
+        extra["partitioned_qwen3_8b_batch64"] = strong_scaling_key(
+            lambda w, r, ag: batched_workload(w, r), args, world, rank, local, peaks)
+        if world == 1:
+            # the other single-GPU configurations: the 32K gated layer (the 70%-of-HBM
+            # target), the short Qwen3-0.6B layer and the GatedDeltaNet step
+            for name in ("qwen35_gated_s32769", "qwen3_0p6b_s1025"):
+                w2 = attention_workload(name, "paged")
+                m2, e2, _ = measure(w2, args, 1, local)
+                extra[name] = summarize(w2, m2, e2, peaks)
+                del w2
+                torch.cuda.empty_cache()
+            w2 = gdn_workload()
+            m2, e2, _ = measure(w2, args, 1, local)
+            extra["qwen35_gdn"] = summarize(w2, m2, e2, peaks)
+            del w2
+            torch.cuda.empty_cache()
     line = {
         "metric": "decode-attn KV-read GB/s" if args.workload != "qwen35_gdn" else "GatedDeltaNet state GB/s",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "us_per_layer": round(per_launch_ms * 1000, 3), "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": dict(workload=args.workload, parallelism=parallelism,
-                       l2="step inputs larger than the 126 MB L2" if total_bytes > (126 << 20)
-                       else "step smaller than L2; consecutive steps re-read it",
-                       **wl["config"]),
+        "config": line_config(args.workload, world),
+        "details": details,
         **extra,
         "e2e": {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2],
-                "ms_per_step": round(ms_e2e, 4)},
-        "roofline": {"bound": "hbm", "kernel": wl["kernel"], "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
+        "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                     "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"],
+                     "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": bpl,
                      "launch_time": ("the kernel's launches timed on their own" if kernel_ms is not None
                                      else "step time / launches per step (includes launch gaps)")
                      + ("; rank 0's bytes over the slowest rank's time" if partitioned_mode else ""),
                      "traffic": traffic},
-        "gpu_launches": wl["launches"] * args.steps,
+        "gpu_launches": launches * args.steps,
         "clocks": clocks,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:

@@ -44,3 +44,23 @@ def test_reference_arm_silent_on_other_ranks(capsys):
     args = argparse.Namespace(workload="qwen35_gdn", steps=4, warmup=1, gpus=2)
     bench.run_reference_arm(args, 2, 1)
     assert capsys.readouterr().out == ""
+
+
+@pytest.mark.parametrize("workload", ["qwen3_8b_s8192", "qwen3_0p6b_s1025", "qwen35_gated_s32769", "qwen3_8b_s131073",
+                                      "qwen35_gdn", "qwen35_pair", "qwen3_8b_batch64"])
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_reference_arm_config_is_this_library_config(workload, world, capsys, monkeypatch):
+    """Both arms print the same `config` for the same workload and N (the reference
+    arm's line is built from line_config too, and nothing run-dependent is in it)."""
+    monkeypatch.setattr(bench, "reference_gpu", lambda *a, **k: {"unavailable": "no GPU"})
+    monkeypatch.setattr(bench, "cpu_baseline", lambda w, budget_s: {
+        "value": 2.0, "unit": "GB/s", "kind": "port", "cores": 1, "sample": w})
+    args = argparse.Namespace(workload=workload, steps=4, warmup=1, gpus=world)
+    bench.run_reference_arm(args, world, 0)
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["config"] == bench.line_config(workload, world)
+    assert line["config"]["workload"] == workload
+    partitioned = world > 1 and workload in ("qwen3_8b_s131073", "qwen3_8b_batch64")
+    assert line["scaling"] == ("strong" if partitioned else "weak")
+    if world == 1:
+        assert line["config"]["parallelism"] == "single"

@@ -4,9 +4,11 @@ Each rank is a spawned process on its own GPU. All ranks build the same seeded
 sequence, keep their own shard (shard_tokens) in their own shuffled page pool, map
 each other's exchange buffers with CUDA IPC (handles exchanged over a gloo process
 group) and call qic_cp_decode_attention three times. Every rank checks its output
-against the whole-sequence call made on its own GPU (max-abs 2e-3 / rel 1e-2) and
-the owner of the last token checks the appended rows byte for byte. Skipped with
-fewer than two GPUs.
+against the whole-sequence call made on its own GPU and against the reference's own
+chain on the whole sequence (head-norm + RoPE of q and k, row copies, paged_attention
+of src/kernels.cu built for sm_100a), both within max-abs 2e-3 / rel 1e-2, and the
+owner of the last token checks the appended rows byte for byte. Skipped with fewer
+than two GPUs.
 """
 import os
 import socket
@@ -49,6 +51,20 @@ def _rank_main(rank, world, port, S, results):
         ws_full = q.Workspace(H, HKV, D, S)
         want = torch.empty(H * D, device="cuda", dtype=qv.dtype)
         q.decode_attention(out=want, **_kw(S, qv, kc_full, vc_full, tab_full, w, kn, vn, True, ws_full))
+        torch.cuda.synchronize()
+        # the reference's chain on the whole sequence, on copies of the caches
+        from oracle.oracle import RefKernels
+
+        ref = RefKernels(qv.dtype)
+        kr, vr = kc_full.clone(), vc_full.clone()
+        lf = (S - 1) // P
+        ref.append_chain(kn, vn, w, 1e-6, 1.0e6, S - 1, kr, vr, HKV, D, int(tab_full[lf]) * P + (S - 1) % P)
+        qr = qv.clone()
+        ref.head_rmsnorm(qr, w, H, D, 1e-6, qr)
+        ref.rope_inplace(qr, H, D, S - 1, 1.0e6)
+        want_ref = torch.empty(H * D, device="cuda", dtype=qv.dtype)
+        ref.paged_attention(qr, kr, vr, tab_full, P, H, HKV, D, S, want_ref)
+        del kr, vr
         t0, t1 = cpm.shard_tokens(S, P, world)[rank]
         n = t1 - t0
         kc, tab = _paged(k[t0:t1], seed=10 + rank)
@@ -65,7 +81,8 @@ def _rank_main(rank, world, port, S, results):
             torch.cuda.synchronize()
             st = ws.status()
             ok, err, idx = allclose_report(out, want, 2e-3, 1e-2)
-            errs.append((call, st, ok, err))
+            ok_r, err_r, _ = allclose_report(out, want_ref, 2e-3, 1e-2)
+            errs.append((call, st, ok and ok_r, max(err, err_r)))
         row_ok = True
         if last:
             lp, lf = (n - 1) // P, (S - 1) // P
