@@ -492,6 +492,80 @@ def cp_workload(world, rank, with_allgather=True, layers=2):
                         "exchange": "in-kernel NVLink stores of tagged words, log-sum-exp merge"})
 
 
+def gemv_workload(layers=4, hidden=4096, inter=12288, q_out=4096, kv_out=1024, seed=7):
+    """The weight-streaming projections of `layers` Qwen3-8B layers (hidden 4096, 32 q
+    heads and 8 kv heads of 128, FFN 12288), four launches per layer chained with
+    programmatic dependent launch: RMSNorm + q/k/v (one launch over three weight
+    buffers), o + residual, RMSNorm + gate/up + SwiGLU, down + residual. Every layer has
+    its own weights (386 MB per layer, more than L2). Bytes = weight bytes + the
+    16-bit inputs, outputs and residuals."""
+    import qwenincuda_b200 as q
+
+    dtype = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(seed)
+
+    def w(k, n):
+        return (torch.randn(k, n, generator=g, device="cuda") * 0.02).to(dtype)
+
+    x = torch.randn(hidden, generator=g, device="cuda").to(dtype)
+    ctx = torch.randn(q_out, generator=g, device="cuda").to(dtype)  # attention output of every layer
+    qb = torch.empty(q_out, device="cuda", dtype=dtype)
+    kb = torch.empty(kv_out, device="cuda", dtype=dtype)
+    vb = torch.empty(kv_out, device="cuda", dtype=dtype)
+    hb = torch.empty(inter, device="cuda", dtype=dtype)
+    ones = torch.ones(hidden, device="cuda", dtype=dtype)
+    lib = q.lib()
+    args, keep = [], []
+    for _ in range(layers):
+        wq, wk, wv, wo = w(hidden, q_out), w(hidden, kv_out), w(hidden, kv_out), w(q_out, hidden)
+        wg, wu, wd = w(hidden, inter), w(hidden, inter), w(inter, hidden)
+        keep += [wq, wk, wv, wo, wg, wu, wd]
+        args += [q.ops.gemv_args(x=x, weights=[wq, wk, wv], outs=[qb, kb, vb], norm_w=ones, pdl=True),
+                 q.ops.gemv_args(x=ctx, weights=[wo], outs=[x], residuals=[x], pdl=True),
+                 q.ops.gemv_args(x=x, weights=[wg, wu], outs=[hb], norm_w=ones, swiglu=True, pdl=True),
+                 q.ops.gemv_args(x=hb, weights=[wd], outs=[x], residuals=[x], pdl=True)]
+    fns = [_call(lib.qic_gemv, a) for a in args]
+
+    def step():
+        for f in fns:
+            f()
+
+    W = [keep[7 * i:7 * i + 7] for i in range(layers)]
+
+    def cublas_step():
+        # the same products through torch's cuBLAS calls, unfused (norms omitted)
+        for wq, wk, wv, wo, wg, wu, wd in W:
+            xr = x.view(1, -1)
+            torch.matmul(xr, wq, out=qb.view(1, -1))
+            torch.matmul(xr, wk, out=kb.view(1, -1))
+            torch.matmul(xr, wv, out=vb.view(1, -1))
+            x.add_(torch.matmul(ctx.view(1, -1), wo).view(-1))
+            hb.copy_((torch.nn.functional.silu(torch.matmul(xr, wg)) * torch.matmul(xr, wu)).view(-1))
+            x.add_(torch.matmul(hb.view(1, -1), wd).view(-1))
+
+    hin = x.cpu().pin_memory()
+    hout = torch.empty_like(x, device="cpu").pin_memory()
+
+    def e2e():
+        x.copy_(hin, non_blocking=True)
+        step()
+        hout.copy_(x, non_blocking=True)
+
+    wbytes = 2 * (hidden * (q_out + 2 * kv_out) + q_out * hidden + 2 * hidden * inter + inter * hidden)
+    vec = 2 * (hidden + (q_out + 2 * kv_out) + q_out + 2 * hidden + hidden + inter + inter + 2 * hidden)
+    per_layer = wbytes + vec
+    splits = [q.ops.gemv_launch_shape(x=x, weights=[wq, wk, wv], outs=[qb, kb, vb], norm_w=ones)[0],
+              q.ops.gemv_launch_shape(x=ctx, weights=[wo], outs=[x], residuals=[x])[0],
+              q.ops.gemv_launch_shape(x=x, weights=[wg, wu], outs=[hb], norm_w=ones, swiglu=True)[0],
+              q.ops.gemv_launch_shape(x=hb, weights=[wd], outs=[x], residuals=[x])[0]]
+    return dict(step=step, bytes=per_layer * layers, launches=4 * layers, bytes_per_launch=per_layer / 4,
+                e2e=(e2e, 2 * hidden, 2 * hidden), kernel="gemv_kernel", status=lambda: 0, keep=(keep, args),
+                library_step=cublas_step,
+                config={"layers": layers, "hidden": hidden, "intermediate": inter, "q_out": q_out, "kv_out": kv_out,
+                        "weight_bytes_per_layer": wbytes, "launches_per_layer": 4, "splits": splits,
+                        "what": "RMSNorm+q/k/v, o+residual, RMSNorm+gate/up+SwiGLU, down+residual"})
+
+
 def time_eager(fn, steps, warmup, world):
     """ms per call of fn (no graph): used for the NCCL all-gather path."""
     for _ in range(warmup):
@@ -758,6 +832,11 @@ def line_config(workload, world):
         c = {"layers": "GatedDeltaNet + gated attention (16/4 heads, d=256, S=32769, paged)"}
         rank_bytes = GdnConfig().state_bytes() + att.kv_read_bytes() + att.append_bytes()
         par = f"replicas{world}" if world > 1 else "single"
+    elif workload == "gemv_qwen3_8b":
+        c = {"layers": 4, "hidden": 4096, "intermediate": 12288, "q_out": 4096, "kv_out": 1024,
+             "launches_per_layer": 4}
+        rank_bytes = 4 * 386 << 20
+        par = f"replicas{world}" if world > 1 else "single"
     elif workload == "qwen3_8b_batch64":
         b = BatchConfig()
         c = {"batch": b.batch, "seq_lens": f"U[{b.min_len},{b.max_len}]+1, seed {b.seed}", "page_size": b.page_size,
@@ -933,6 +1012,9 @@ def main():
     elif args.workload == "qwen3_8b_batch64":
         wl = batched_workload(world, rank)
         ms, ms_e2e, clocks = measure(wl, args, world, local)
+    elif args.workload == "gemv_qwen3_8b" and args.no_extra:
+        wl = gemv_workload(args.layers or 4)  # profiling runs of the projections alone
+        ms, ms_e2e, clocks = measure(wl, args, world, local)
     else:
         raise SystemExit(f"unknown workload {args.workload}")
 
@@ -976,6 +1058,20 @@ def main():
             w2 = gdn_workload()
             m2, e2, _ = measure(w2, args, 1, local)
             extra["qwen35_gdn"] = summarize(w2, m2, e2, peaks)
+            del w2
+            torch.cuda.empty_cache()
+            # the projections around the attention of the same model (weight bytes)
+            w2 = gemv_workload()
+            m2, e2, _ = measure(w2, args, 1, local)
+            extra["gemv_qwen3_8b"] = summarize(w2, m2, e2, peaks)
+            extra["gemv_qwen3_8b"]["us_per_model_layer"] = round(m2 * 1000 / w2["config"]["layers"], 2)
+            gl = capture(w2["library_step"])
+            ml = time_graph(gl, args.steps, args.warmup, 1)
+            del gl
+            extra["gemv_qwen3_8b"]["torch_cublas_unfused"] = {
+                "value": round(w2["bytes"] / (ml * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "us_per_model_layer": round(ml * 1000 / w2["config"]["layers"], 2),
+                "what": "the same products as torch.matmul (cuBLAS) calls with separate SiLU, multiply and adds"}
             del w2
             torch.cuda.empty_cache()
     line = {

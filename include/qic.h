@@ -333,6 +333,59 @@ int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv
 int qic_batch_decode_attention(const qic_batch_decode_args* args, qic_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* Weight-streaming GEMV projections of one token, fused with the neighbouring */
+/* RMSNorm, SwiGLU and residual add.                                           */
+/* ------------------------------------------------------------------------- */
+
+#define QIC_GEMV_MAX_SEGMENTS 4
+
+/* Flags of qic_gemv_args.flags (QIC_PDL = 4 is accepted too: the kernel may start
+ * while the previous kernel in the stream runs and load its first weight rows; x,
+ * norm_w and the residuals are read after that kernel has completed). */
+enum {
+  QIC_GEMV_RMSNORM = 1,   /* x := T(x * rsqrt(mean(x^2) + eps) * norm_w) first (launch_rmsnorm) */
+  QIC_GEMV_SWIGLU = 2,    /* two segments of equal out_dim, gate then up: seg[0].out = T(silu(gate) * up)
+                             from the 16-bit gate and up (launch_swiglu); seg[1].out is not written */
+  QIC_GEMV_RESIDUAL = 8   /* seg[k].out = T(T(product) + seg[k].residual) (launch_add_inplace);
+                             residual may be the same buffer as out */
+};
+
+typedef struct qic_gemv_segment {
+  const void* w;          /* [in_dim, out_dim], out_dim contiguous: element (i, o) at w[i*out_dim + o],
+                             the reference's column-major weights (lda = out_dim); 16-byte aligned */
+  void* out;              /* [out_dim] */
+  const void* residual;   /* [out_dim] (QIC_GEMV_RESIDUAL) */
+  int32_t out_dim;        /* multiple of 8 */
+  int32_t reserved;
+} qic_gemv_segment;
+
+typedef struct qic_gemv_args {
+  int32_t dtype;          /* QIC_DTYPE_*: x, weights, outputs */
+  int32_t in_dim;         /* K, 1..131072 */
+  int32_t num_segments;   /* projections of the same x in this launch, 1..QIC_GEMV_MAX_SEGMENTS */
+  uint32_t flags;         /* QIC_GEMV_*, QIC_PDL */
+  const void* x;          /* [in_dim]; must not overlap any out */
+  const void* norm_w;     /* [in_dim] (QIC_GEMV_RMSNORM) */
+  float eps;              /* RMSNorm epsilon */
+  int32_t splits;         /* CTAs splitting the rows of a column tile (one cluster), 1..16; 0 = chosen */
+  qic_gemv_segment seg[QIC_GEMV_MAX_SEGMENTS];
+} qic_gemv_args;
+
+/* seg[k].out[o] = T(sum_i x[i] * seg[k].w[i*out_dim + o]) with fp32 accumulation, for every
+ * segment, in one launch, optionally with the input RMSNorm, the SwiGLU of a gate/up pair and
+ * the residual add fused. Replaces QwenMiniModel::gemv (src/model.cpp:603-617: cublasGemmEx, one
+ * column, fp32 compute) and, with the flags, launch_rmsnorm -> gemv of q, k and v (or of the
+ * linear layer's qkv, z, b, a) (src/model.cpp:832, 627-631, 667-670), launch_rmsnorm -> gemv(w_gate),
+ * gemv(w_up) -> launch_swiglu (src/model.cpp:800-804), gemv(w_down) -> launch_add_inplace
+ * (src/model.cpp:805-806) and gemv(wo / out_proj) -> launch_add_inplace (src/model.cpp:653 or 794,
+ * then 840), with the residual copies (src/model.cpp:799, 831) dropped. Deterministic: the same
+ * inputs give the same bits on every call. Allocates nothing. */
+int qic_gemv(const qic_gemv_args* args, qic_stream_t stream);
+
+/* The split count qic_gemv uses for these arguments (its own choice when args->splits is 0). */
+int qic_gemv_launch_shape(const qic_gemv_args* args, int* splits, int* tiles);
+
+/* ------------------------------------------------------------------------- */
 /* Qwen3.5 GatedDeltaNet decode step (state resident on the device).          */
 /* ------------------------------------------------------------------------- */
 

@@ -7,6 +7,8 @@
   reference's own src/kernels.cu compiled unchanged for sm_100a (oracle/Makefile).
   Takes CUDA torch tensors; launches on the legacy default stream like the
   reference and synchronises.
+* ``RefModel``: the reference model's gemv and FFN block members from the same
+  libraries as ``RefGatedDelta`` (CUDA tensors in).
 * ``RefGatedDelta``: ctypes binding of oracle/_ref/libqicref_gdn{,_bf16}.so, the
   reference's own GatedDeltaNet decode step (src/model.cpp:656-795, compiled unchanged
   inside oracle/ref_gdn_harness.cpp; fp16, or the bfloat16 instance). Takes and returns
@@ -156,6 +158,9 @@ class RefKernels:
         lib.qicref_flash_attention.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _vp]
         lib.qicref_paged_attention.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]
         lib.qicref_copy_row.argtypes = [_vp, _vp, ctypes.c_longlong, _i]
+        lib.qicref_rmsnorm.argtypes = [_vp, _vp, _i, _f, _vp]
+        lib.qicref_add_inplace.argtypes = [_vp, _vp, _i]
+        lib.qicref_swiglu.argtypes = [_vp, _vp, _i, _vp]
         self.lib = lib
         self.dtype = dtype
 
@@ -208,6 +213,21 @@ class RefKernels:
                   "paged_attention")
         if sync:
             self.sync()
+
+    def rmsnorm(self, x, w, n, eps, out):
+        torch.cuda.synchronize()
+        self._chk(self.lib.qicref_rmsnorm(_p(x), _p(w), n, eps, _p(out)), "rmsnorm")
+        self.sync()
+
+    def add_inplace(self, x, y, n):
+        torch.cuda.synchronize()
+        self._chk(self.lib.qicref_add_inplace(_p(x), _p(y), n), "add_inplace")
+        self.sync()
+
+    def swiglu(self, gate, up, n, out):
+        torch.cuda.synchronize()
+        self._chk(self.lib.qicref_swiglu(_p(gate), _p(up), n, _p(out)), "swiglu")
+        self.sync()
 
     def append_chain(self, k_new, v_new, k_norm_w, eps, theta, position, k_cache, v_cache, num_kv_heads, head_dim,
                      slot):
@@ -268,6 +288,36 @@ class RefGatedDelta:
         device, cuBLAS handle), for repeated steps; close() releases it."""
         return _RefGatedDeltaLayer(self.lib, self.dtype, conv_w, dt_bias, a_log, norm_w, conv_state,
                                    recurrent_state, num_k_heads, num_v_heads, k_head_dim, v_head_dim, conv_kernel, eps)
+
+
+class RefModel:
+    """The reference model's projection members run on CUDA tensors: QwenMiniModel::gemv
+    (src/model.cpp:603-617, cuBLAS with the reference's arguments) and run_ffn_block
+    (src/model.cpp:797-807), compiled unchanged into oracle/_ref/libqicref_gdn{,_bf16}.so."""
+
+    def __init__(self, dtype: torch.dtype = torch.float16):
+        self.dtype = dtype
+        path = REF_DIR / ("libqicref_gdn.so" if dtype == torch.float16 else "libqicref_gdn_bf16.so")
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref REF=<reference project root>)")
+        lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
+        lib.qicref_gemv.argtypes = [_vp, _vp, _i, _i, _vp]
+        lib.qicref_gemv.restype = _i
+        lib.qicref_ffn_block.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _f]
+        lib.qicref_ffn_block.restype = _i
+        self.lib = lib
+
+    def gemv(self, x, w, in_dim, out_dim, out):
+        """out = the reference's gemv of x with w [in_dim, out_dim] (out_dim contiguous)."""
+        torch.cuda.synchronize()
+        if self.lib.qicref_gemv(_p(x), _p(w), in_dim, out_dim, _p(out)) != 0:
+            raise RuntimeError("reference gemv failed")
+
+    def ffn_block(self, x, ffn_norm, w_gate, w_up, w_down, hidden, inter, eps):
+        """x (in place) = the reference's FFN block of x."""
+        torch.cuda.synchronize()
+        if self.lib.qicref_ffn_block(_p(x), _p(ffn_norm), _p(w_gate), _p(w_up), _p(w_down), hidden, inter, eps) != 0:
+            raise RuntimeError("reference FFN block failed")
 
 
 class _RefGatedDeltaLayer:

@@ -180,3 +180,80 @@ extern "C" int qicref_gdn_step(int Hk, int Hv, int dk, int dv, int K, float eps,
   qicref_gdn_destroy(h);
   return rc;
 }
+
+// ---------------------------------------------------------------------------
+// The reference's projections: QwenMiniModel::gemv (src/model.cpp:603-617, cuBLAS
+// with the reference's own arguments) and run_ffn_block (src/model.cpp:797-807), run
+// on caller device buffers through one model object whose cuBLAS handle is created
+// once, as the reference's load() does. The model's runtime buffers that these
+// members use are set to caller or scratch memory; free_all() never sees them.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct RefProj {
+  QwenMiniModel m;
+  std::vector<void*> scratch;
+  RefProj() { CUBLAS_CHECK(cublasCreate(&m.cublas_)); }
+  ~RefProj() {
+    m.x_ = m.x_resid_ = m.x_norm_ = m.ffn_gate_ = m.ffn_up_ = m.ffn_hidden_ = nullptr;
+    for (void* p : scratch) cudaFree(p);
+  }
+  half* buf(size_t elems) {
+    void* p = nullptr;
+    CUDA_CHECK(cudaMalloc(&p, elems * sizeof(half)));
+    scratch.push_back(p);
+    return static_cast<half*>(p);
+  }
+};
+
+RefProj* ref_proj() {
+  static RefProj* r = new RefProj();  // kept until exit, like the reference's model
+  return r;
+}
+
+}  // namespace
+
+// out[out_dim] = the reference's gemv of x[in_dim] with w[in_dim, out_dim] (device buffers).
+extern "C" int qicref_gemv(const void* x, const void* w, int in_dim, int out_dim, void* out) {
+  try {
+    ref_proj()->m.gemv(static_cast<const half*>(x), static_cast<const half*>(w), in_dim, out_dim,
+                       static_cast<half*>(out));
+    CUDA_CHECK(cudaDeviceSynchronize());
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "reference gemv failed: %s\n", e.what());
+    return 1;
+  }
+  return 0;
+}
+
+// x[hidden] (device, in place) = the reference's FFN block: x + down(swiglu(gate(norm(x)), up(norm(x)))).
+extern "C" int qicref_ffn_block(void* x, const void* ffn_norm, const void* w_gate, const void* w_up, const void* w_down,
+                                int hidden, int inter, float eps) {
+  try {
+    RefProj* r = ref_proj();
+    QwenMiniModel& m = r->m;
+    m.cfg_.hidden_size = hidden;
+    m.cfg_.intermediate_size = inter;
+    m.cfg_.rms_norm_eps = eps;
+    m.x_ = static_cast<half*>(x);
+    m.x_resid_ = r->buf(hidden);
+    m.x_norm_ = r->buf(hidden);
+    m.ffn_gate_ = r->buf(inter);
+    m.ffn_up_ = r->buf(inter);
+    m.ffn_hidden_ = r->buf(inter);
+    QwenMiniModel::LayerWeights lw;
+    lw.ffn_norm = const_cast<half*>(static_cast<const half*>(ffn_norm));
+    lw.w_gate = const_cast<half*>(static_cast<const half*>(w_gate));
+    lw.w_up = const_cast<half*>(static_cast<const half*>(w_up));
+    lw.w_down = const_cast<half*>(static_cast<const half*>(w_down));
+    m.run_ffn_block(lw);
+    CUDA_CHECK(cudaDeviceSynchronize());
+    m.x_ = m.x_resid_ = m.x_norm_ = m.ffn_gate_ = m.ffn_up_ = m.ffn_hidden_ = nullptr;
+    for (void* p : r->scratch) cudaFree(p);
+    r->scratch.clear();
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "reference FFN block failed: %s\n", e.what());
+    return 1;
+  }
+  return 0;
+}

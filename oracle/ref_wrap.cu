@@ -54,6 +54,21 @@ int qicref_copy_row(void* cache, const void* row, long long row_index, int kv_di
   return static_cast<int>(cudaMemcpy(dst, row, bytes, cudaMemcpyDeviceToDevice));
 }
 
+int qicref_rmsnorm(const void* x, const void* w, int n, float eps, void* out) {
+  launch_rmsnorm(static_cast<const half*>(x), static_cast<const half*>(w), n, eps, static_cast<half*>(out));
+  return static_cast<int>(cudaGetLastError());
+}
+
+int qicref_add_inplace(void* x, const void* y, int n) {
+  launch_add_inplace(static_cast<half*>(x), static_cast<const half*>(y), n);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int qicref_swiglu(const void* gate, const void* up, int n, void* out) {
+  launch_swiglu(static_cast<const half*>(gate), static_cast<const half*>(up), n, static_cast<half*>(out));
+  return static_cast<int>(cudaGetLastError());
+}
+
 int qicref_synchronize(void) { return static_cast<int>(cudaDeviceSynchronize()); }
 
 }  // extern "C"

@@ -32,6 +32,7 @@ from .ops import (  # noqa: F401
     batch_decode_attention,
     decode_attention,
     gated_delta_decode,
+    gemv,
     kv_append,
     launch_flash_attention,
     launch_head_rmsnorm,
@@ -53,6 +54,7 @@ __all__ = [
     "Workspace",
     "decode_attention",
     "gated_delta_decode",
+    "gemv",
     "kv_append",
     "launch_flash_attention",
     "launch_head_rmsnorm",

@@ -162,6 +162,40 @@ class GdnArgs(ctypes.Structure):
     ]
 
 
+QIC_GEMV_MAX_SEGMENTS = 4
+QIC_GEMV_RMSNORM = 1
+QIC_GEMV_SWIGLU = 2
+QIC_GEMV_RESIDUAL = 8
+
+
+class GemvSegment(ctypes.Structure):
+    """Mirror of qic_gemv_segment."""
+
+    _fields_ = [
+        ("w", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("out_dim", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class GemvArgs(ctypes.Structure):
+    """Mirror of qic_gemv_args."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("in_dim", ctypes.c_int32),
+        ("num_segments", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("x", ctypes.c_void_p),
+        ("norm_w", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("splits", ctypes.c_int32),
+        ("seg", GemvSegment * QIC_GEMV_MAX_SEGMENTS),
+    ]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -187,6 +221,9 @@ SIGNATURES = {
     "qic_decode_launch_shape": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(ctypes.c_int),
                                                ctypes.POINTER(ctypes.c_int)]),
     "qic_gated_delta_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), _vp]),
+    "qic_gemv": (ctypes.c_int, [ctypes.POINTER(GemvArgs), _vp]),
+    "qic_gemv_launch_shape": (ctypes.c_int, [ctypes.POINTER(GemvArgs), ctypes.POINTER(ctypes.c_int),
+                                             ctypes.POINTER(ctypes.c_int)]),
     "qic_batch_plan": (
         ctypes.c_int,
         [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,

@@ -33,6 +33,7 @@ UNITS = [
     ("capi.cpp", []),
     ("compat.cu", ["--use_fast_math"]),
     ("noalloc.cu", []),
+    ("gemv_kernel.cu", ["--use_fast_math"]),
 ]
 
 

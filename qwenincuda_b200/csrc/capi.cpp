@@ -196,6 +196,8 @@ int qic_workspace_status(void* workspace, qic_stream_t stream, int* dev_status) 
   return QIC_SUCCESS;
 }
 
+}  // extern "C"
+
 namespace {
 
 // Shared checks of the single and batched decode entry points.
@@ -259,6 +261,10 @@ int box_height(bool paged, int page_size, int tok, int* log2) {
 }
 
 }  // namespace
+
+extern "C" {
+
+}  // extern "C"
 
 namespace {
 
@@ -437,6 +443,8 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
 }
 
 }  // namespace
+
+extern "C" {
 
 int qic_decode_attention(const qic_decode_args* a, qic_stream_t stream) {
   return decode_attention_impl(a, nullptr, stream);
@@ -650,6 +658,108 @@ int qic_batch_decode_attention(const qic_batch_decode_args* a, qic_stream_t stre
   p.n_splits = a->plan_items;  // grid size
   p.cluster = 1;
   return cuda_status(qic::launch_decode_attention(a->dtype, D, p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"
+
+namespace {
+
+bool ranges_overlap(const void* a, size_t an, const void* b, size_t bn) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + bn && b0 < a0 + an;
+}
+
+// Checks a GEMV call and fills the kernel parameters (without the split count).
+int gemv_prepare(const qic_gemv_args* a, qic::GemvParams* p, bool* pair, bool* norm) {
+  if (a == nullptr || !valid_dtype(a->dtype)) return QIC_ERROR_INVALID_VALUE;
+  const int K = a->in_dim, ns = a->num_segments;
+  const uint32_t known = QIC_GEMV_RMSNORM | QIC_GEMV_SWIGLU | QIC_GEMV_RESIDUAL | QIC_PDL;
+  if (K <= 0 || ns < 1 || ns > qic::kGemvMaxSegments || (a->flags & ~known) != 0 || a->x == nullptr)
+    return QIC_ERROR_INVALID_VALUE;
+  if (K > qic::kGemvMaxSplits * qic::kGemvMaxRowsPerSplit) return QIC_ERROR_NOT_SUPPORTED;
+  if (a->splits < 0 || a->splits > qic::kGemvMaxSplits) return QIC_ERROR_INVALID_VALUE;
+  *pair = (a->flags & QIC_GEMV_SWIGLU) != 0;
+  *norm = (a->flags & QIC_GEMV_RMSNORM) != 0;
+  const bool res = (a->flags & QIC_GEMV_RESIDUAL) != 0;
+  if (*pair && (ns != 2 || res || a->seg[0].out_dim != a->seg[1].out_dim)) return QIC_ERROR_INVALID_VALUE;
+  if (*norm && a->norm_w == nullptr) return QIC_ERROR_INVALID_VALUE;
+  if (!aligned2(a->x) || (*norm && !aligned2(a->norm_w))) return QIC_ERROR_MISALIGNED;
+  std::memset(p, 0, sizeof(*p));
+  long long tiles = 0;
+  for (int k = 0; k < ns; ++k) {
+    const qic_gemv_segment& g = a->seg[k];
+    if (g.w == nullptr || g.out_dim <= 0 || (g.out_dim % 8) != 0 || (g.out == nullptr && !(*pair && k == 1)) ||
+        (res && g.residual == nullptr))
+      return QIC_ERROR_INVALID_VALUE;
+    if (!aligned16(g.w) || (g.out != nullptr && !aligned2(g.out)) || (res && !aligned2(g.residual)))
+      return QIC_ERROR_MISALIGNED;
+    // every CTA reads the whole input while others write their outputs
+    if (g.out != nullptr && ranges_overlap(a->x, static_cast<size_t>(K) * 2, g.out, static_cast<size_t>(g.out_dim) * 2))
+      return QIC_ERROR_INVALID_VALUE;
+    p->seg[k].w = g.w;
+    p->seg[k].out = g.out;
+    p->seg[k].res = res ? g.residual : nullptr;
+    p->seg[k].N = g.out_dim;
+    p->seg[k].tile0 = static_cast<int>(tiles);
+    if (!(*pair && k == 1)) tiles += (g.out_dim + qic::kGemvTile - 1) / qic::kGemvTile;
+  }
+  if (*pair) p->seg[1].tile0 = INT32_MAX;  // both halves of the pair share the tiles of segment 0
+  if (tiles > 65535) return QIC_ERROR_NOT_SUPPORTED;
+  p->x = a->x;
+  p->norm_w = *norm ? a->norm_w : nullptr;
+  p->eps = a->eps;
+  p->K = K;
+  p->flags = static_cast<int>(a->flags & QIC_PDL);
+  p->nseg = ns;
+  p->n_tiles = static_cast<int>(tiles);
+  return QIC_SUCCESS;
+}
+
+// Rows of a tile per CTA when `splits` CTAs share them (multiple of 8).
+int gemv_rows_per_split(int K, int splits) { return ((K + splits - 1) / splits + 7) / 8 * 8; }
+
+// Split count: the caller's, else the largest cluster size (at most 16, at least 64 rows
+// per CTA, rows fitting shared memory) at which every tile's cluster is resident at once.
+int gemv_splits(const qic_gemv_args* a, int n_tiles) {
+  const int K = a->in_dim;
+  const int min_c = (K + qic::kGemvMaxRowsPerSplit - 1) / qic::kGemvMaxRowsPerSplit;
+  if (a->splits > 0) return std::max(a->splits, min_c);
+  int best = 0;
+  for (int c = std::max(1, min_c); c <= qic::kGemvMaxSplits; ++c) {
+    if (c > 1 && K < 64 * c) break;
+    const int m = qic::gemv_max_active_clusters(a->dtype, c, gemv_rows_per_split(K, c));
+    if (m > 0 && n_tiles <= m) best = c;
+  }
+  if (best == 0) best = std::max(1, min_c);  // more tiles than one wave holds: several waves
+  return best;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qic_gemv_launch_shape(const qic_gemv_args* a, int* splits, int* tiles) {
+  if (splits == nullptr || tiles == nullptr) return QIC_ERROR_INVALID_VALUE;
+  qic::GemvParams p;
+  bool pair = false, norm = false;
+  const int rc = gemv_prepare(a, &p, &pair, &norm);
+  if (rc != QIC_SUCCESS) return rc;
+  *splits = gemv_splits(a, p.n_tiles);
+  *tiles = p.n_tiles;
+  return QIC_SUCCESS;
+}
+
+int qic_gemv(const qic_gemv_args* a, qic_stream_t stream) {
+  qic::GemvParams p;
+  bool pair = false, norm = false;
+  int rc = gemv_prepare(a, &p, &pair, &norm);
+  if (rc != QIC_SUCCESS) return rc;
+  p.splits = gemv_splits(a, p.n_tiles);
+  if (p.splits > qic::kGemvMaxSplits) return QIC_ERROR_NOT_SUPPORTED;
+  p.rows_per_split = gemv_rows_per_split(a->in_dim, p.splits);
+  if (p.rows_per_split > qic::kGemvMaxRowsPerSplit) return QIC_ERROR_NOT_SUPPORTED;
+  p.xs_floats = p.rows_per_split;  // a multiple of 8
+  return cuda_status(qic::launch_gemv(a->dtype, p, pair, norm, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int qic_gated_delta_decode(const qic_gdn_args* a, qic_stream_t stream) {

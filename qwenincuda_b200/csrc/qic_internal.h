@@ -107,6 +107,42 @@ struct AttnParams {
   void* cp_peer[kMaxRanks];          // every rank's exchange buffer, addressable here
 };
 
+// Weight-streaming GEMV (gemv_kernel.cu): 256 threads per CTA, 256-column tiles, up to
+// kGemvMaxSegments projections of one input per launch, the rows of a tile split over
+// a thread-block cluster of up to kGemvMaxSplits CTAs.
+constexpr int kGemvThreads = 256;
+constexpr int kGemvTile = 256;
+constexpr int kGemvMaxSegments = QIC_GEMV_MAX_SEGMENTS;
+constexpr int kGemvMaxSplits = 16;
+constexpr int kGemvMaxRowsPerSplit = 8192;  // normalised input rows kept in shared memory
+
+struct GemvSeg {
+  const void* w;    // [K, N], N contiguous
+  void* out;        // [N]
+  const void* res;  // [N] residual or null
+  int N;
+  int tile0;        // first tile of this segment in the grid
+};
+
+struct GemvParams {
+  const void* x;       // [K]
+  const void* norm_w;  // [K] or null
+  float eps;
+  int K;
+  int flags;           // QIC_PDL
+  int nseg;
+  int n_tiles;
+  int splits;          // CTAs per cluster along the rows
+  int rows_per_split;
+  int xs_floats;       // floats of the input slice in shared memory (rows_per_split rounded up to 8)
+  GemvSeg seg[kGemvMaxSegments];
+};
+
+cudaError_t launch_gemv(int dtype, const GemvParams& p, bool pair, bool norm, cudaStream_t stream);
+size_t gemv_smem_bytes(int rows_per_split);
+// Clusters of `cluster` GEMV CTAs resident at once (-1 or 0 if unknown).
+int gemv_max_active_clusters(int dtype, int cluster, int rows_per_split);
+
 // Launchers (attn_kernel.cu)
 cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p, cudaStream_t stream);
 // out = log-sum-exp merge of n partials [n][Hkv][partial_floats] (+ gate)

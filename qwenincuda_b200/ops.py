@@ -290,3 +290,56 @@ def batch_decode_attention(stream=None, **kw):
     """Batched paged decode over a shared page pool; see qic_batch_decode_attention."""
     a = batch_decode_args(**kw)
     check(lib().qic_batch_decode_attention(ctypes.byref(a), _stream(stream)), "qic_batch_decode_attention")
+
+
+def gemv_args(*, x, weights, outs, residuals=None, norm_w=None, eps=1e-6, swiglu=False, pdl=False,
+              splits=0) -> "GemvArgs":
+    """qic_gemv_args for one launch: x [K]; weights: list of [K, N_k] tensors (N_k
+    contiguous, the reference's column-major layout); outs: list of [N_k] outputs (with
+    swiglu, weights = [w_gate, w_up] and outs = [out], silu(gate)*up); residuals: list
+    of [N_k] tensors added to the products (may be the outs themselves); norm_w: fuse
+    the RMSNorm of x with this weight."""
+    from .abi import QIC_GEMV_MAX_SEGMENTS, QIC_GEMV_RESIDUAL, QIC_GEMV_RMSNORM, QIC_GEMV_SWIGLU, GemvArgs
+
+    if not 1 <= len(weights) <= QIC_GEMV_MAX_SEGMENTS:
+        raise ValueError(f"1..{QIC_GEMV_MAX_SEGMENTS} weight segments")
+    outs = list(outs) + [None] * (len(weights) - len(outs))
+    a = GemvArgs()
+    a.dtype = dtype_code(x)
+    a.in_dim = x.numel()
+    a.num_segments = len(weights)
+    a.x = _ptr(x)
+    a.eps = eps
+    a.splits = splits
+    flags = QIC_PDL if pdl else 0
+    if norm_w is not None:
+        flags |= QIC_GEMV_RMSNORM
+        a.norm_w = _ptr(norm_w)
+    if swiglu:
+        flags |= QIC_GEMV_SWIGLU
+    if residuals is not None:
+        flags |= QIC_GEMV_RESIDUAL
+    for k, w in enumerate(weights):
+        if w.dim() != 2 or w.shape[0] != a.in_dim or not w.is_contiguous():
+            raise ValueError(f"weight {k}: a contiguous [{a.in_dim}, N] tensor")
+        a.seg[k].w = _ptr(w)
+        a.seg[k].out_dim = w.shape[1]
+        a.seg[k].out = _ptr(outs[k])
+        if residuals is not None:
+            a.seg[k].residual = _ptr(residuals[k])
+    a.flags = flags
+    return a
+
+
+def gemv(stream=None, **kw) -> None:
+    """Weight-streaming GEMV projections of one token; see qic_gemv in include/qic.h."""
+    a = gemv_args(**kw)
+    check(lib().qic_gemv(ctypes.byref(a), _stream(stream)), "qic_gemv")
+
+
+def gemv_launch_shape(**kw) -> tuple[int, int]:
+    """(splits, column tiles) qic_gemv uses for these arguments."""
+    a = gemv_args(**kw)
+    s, t = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().qic_gemv_launch_shape(ctypes.byref(a), ctypes.byref(s), ctypes.byref(t)), "qic_gemv_launch_shape")
+    return s.value, t.value
