@@ -226,7 +226,7 @@ def _call(fn, args_struct):
 # workloads: each returns dict(step=callable, bytes=int, launches=int per step,
 # e2e=(callable, h2d, d2h), kernel=name, status=callable, config=dict)
 # ---------------------------------------------------------------------------
-def attention_workload(name, layout, layers=None):
+def attention_workload(name, layout, layers=None, splits=0):
     import qwenincuda_b200 as q
     from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
 
@@ -250,7 +250,7 @@ def attention_workload(name, layout, layers=None):
             page_table=inp.page_table[layer] if inp.paged else None, page_size=cfg.page_size,
             q_norm_w=inp.q_norm_w, k_norm_w=inp.k_norm_w, k_new=inp.k_new[layer], v_new=inp.v_new[layer],
             eps=cfg.eps, rope_theta=cfg.rope_theta, fuse_q=True, fuse_append=True, workspace=ws,
-            cache_tokens=inp.cache_tokens, pdl=True, q_gate_interleaved=gated)
+            cache_tokens=inp.cache_tokens, pdl=True, q_gate_interleaved=gated, num_splits=splits)
         fns.append(_call(q.lib().qic_decode_attention, a))
 
     def step():
@@ -973,6 +973,7 @@ def main():
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling runs only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="only the requested workload (profiling runs)")
+    ap.add_argument("--splits", type=int, default=0, help="attention splits per kv head (tuning runs; 0 = chosen)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
@@ -993,7 +994,7 @@ def main():
         if "allgather_nccl_path" in res:
             extra["allgather_nccl_path"] = res["allgather_nccl_path"]
     elif args.workload in ATTN_WORKLOADS:
-        wl = attention_workload(args.workload, "paged", args.layers)
+        wl = attention_workload(args.workload, "paged", args.layers, args.splits)
         ms, ms_e2e, clocks = measure(wl, args, world, local)
         if world == 1 and not args.no_extra:
             extra["e2e_eager"] = eager_e2e(wl, args)

@@ -369,6 +369,8 @@ typedef struct qic_gemv_args {
   float eps;              /* RMSNorm epsilon */
   int32_t splits;         /* CTAs splitting the rows of a column tile (one cluster), 1..16; 0 = chosen */
   qic_gemv_segment seg[QIC_GEMV_MAX_SEGMENTS];
+  void* status;           /* device int32 status word (QIC_DEV_TIMEOUT is OR-ed in when a bounded wait
+                             for a weight copy gives up; the outputs are then not written), or NULL */
 } qic_gemv_args;
 
 /* seg[k].out[o] = T(sum_i x[i] * seg[k].w[i*out_dim + o]) with fp32 accumulation, for every

@@ -193,6 +193,7 @@ class GemvArgs(ctypes.Structure):
         ("eps", ctypes.c_float),
         ("splits", ctypes.c_int32),
         ("seg", GemvSegment * QIC_GEMV_MAX_SEGMENTS),
+        ("status", ctypes.c_void_p),
     ]
 
 

@@ -105,6 +105,23 @@ int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens,
   return r == CUDA_SUCCESS ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
 }
 
+// GEMV weights [K rows, N columns] (N contiguous) as a 2D tensor {N, K}; one box is
+// kGemvTile columns of kGemvRowsPerSlot rows, row-major in shared memory, zeros past
+// either edge.
+int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int K, int N) {
+  load_driver_entry_points();
+  if (g_encode == nullptr) return QIC_ERROR_CUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(qic::kGemvTile), static_cast<cuuint32_t>(qic::kGemvRowsPerSlot)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, dtype == QIC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
+}
+
 bool valid_dtype(int d) { return d == QIC_DTYPE_F16 || d == QIC_DTYPE_BF16; }
 bool supported_head_dim(int d) { return d == 64 || d == 128 || d == 256; }
 
@@ -683,7 +700,8 @@ int gemv_prepare(const qic_gemv_args* a, qic::GemvParams* p, bool* pair, bool* n
   const bool res = (a->flags & QIC_GEMV_RESIDUAL) != 0;
   if (*pair && (ns != 2 || res || a->seg[0].out_dim != a->seg[1].out_dim)) return QIC_ERROR_INVALID_VALUE;
   if (*norm && a->norm_w == nullptr) return QIC_ERROR_INVALID_VALUE;
-  if (!aligned2(a->x) || (*norm && !aligned2(a->norm_w))) return QIC_ERROR_MISALIGNED;
+  if (!aligned2(a->x) || (*norm && !aligned2(a->norm_w)) || (reinterpret_cast<uintptr_t>(a->status) & 3u))
+    return QIC_ERROR_MISALIGNED;
   std::memset(p, 0, sizeof(*p));
   long long tiles = 0;
   for (int k = 0; k < ns; ++k) {
@@ -718,20 +736,28 @@ int gemv_prepare(const qic_gemv_args* a, qic::GemvParams* p, bool* pair, bool* n
 // Rows of a tile per CTA when `splits` CTAs share them (multiple of 8).
 int gemv_rows_per_split(int K, int splits) { return ((K + splits - 1) / splits + 7) / 8 * 8; }
 
-// Split count: the caller's, else the largest cluster size (at most 16, at least 64 rows
-// per CTA, rows fitting shared memory) at which every tile's cluster is resident at once.
+// Split count: the caller's, else the largest cluster size from {16, 12, 8, 6, 5, 4, 3,
+// 2, 1} (at least 64 rows per CTA, rows fitting shared memory) that keeps the grid at
+// most 5/3 CTAs per SM with every tile's cluster resident at once. Swept on the
+// Qwen3-8B projections (8 chained launches each, GB/s): q/k/v 24 tiles, splits 8 /
+// 10 / 12 -> 4619 / 4361 / 3638; o 16 tiles, 12 / 13 / 16 -> 4000 / 3862 / 3023;
+// gate/up 48 tiles, 5 / 6 -> 6152 / 4528; down 16 tiles, 12 / 13 -> 5446 / 4693. More
+// CTAs (odd cluster sizes, or 2 per SM everywhere) left some clusters to a second
+// wave behind the preceding launch's CTAs.
 int gemv_splits(const qic_gemv_args* a, int n_tiles) {
   const int K = a->in_dim;
   const int min_c = (K + qic::kGemvMaxRowsPerSplit - 1) / qic::kGemvMaxRowsPerSplit;
   if (a->splits > 0) return std::max(a->splits, min_c);
-  int best = 0;
-  for (int c = std::max(1, min_c); c <= qic::kGemvMaxSplits; ++c) {
-    if (c > 1 && K < 64 * c) break;
+  static const int kSizes[] = {16, 12, 8, 6, 5, 4, 3, 2, 1};
+  const long long cap = std::max<long long>(n_tiles, static_cast<long long>(sm_count()) * 5 / 3);
+  for (int c : kSizes) {
+    if (c < min_c) break;
+    if (c > 1 && K < 64 * c) continue;
+    if (static_cast<long long>(n_tiles) * c > cap) continue;
     const int m = qic::gemv_max_active_clusters(a->dtype, c, gemv_rows_per_split(K, c));
-    if (m > 0 && n_tiles <= m) best = c;
+    if (m > 0 && n_tiles <= m) return c;
   }
-  if (best == 0) best = std::max(1, min_c);  // more tiles than one wave holds: several waves
-  return best;
+  return std::max(1, min_c);  // more tiles than one wave holds: several waves
 }
 
 }  // namespace
@@ -754,6 +780,12 @@ int qic_gemv(const qic_gemv_args* a, qic_stream_t stream) {
   bool pair = false, norm = false;
   int rc = gemv_prepare(a, &p, &pair, &norm);
   if (rc != QIC_SUCCESS) return rc;
+  for (int k = 0; k < a->num_segments; ++k) {
+    rc = encode_weight_map(&p.tm[k], a->dtype, a->seg[k].w, a->in_dim, a->seg[k].out_dim);
+    if (rc != QIC_SUCCESS) return rc;
+  }
+  p.status = static_cast<int*>(a->status);
+  p.timeout_ns = timeout_ns();
   p.splits = gemv_splits(a, p.n_tiles);
   if (p.splits > qic::kGemvMaxSplits) return QIC_ERROR_NOT_SUPPORTED;
   p.rows_per_split = gemv_rows_per_split(a->in_dim, p.splits);

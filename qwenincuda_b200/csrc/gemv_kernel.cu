@@ -14,11 +14,16 @@
 //
 // Design
 //  * A CTA (8 warps) owns a 256-column tile of one segment (or, for SwiGLU, the same
-//    256 columns of gate and up) and a contiguous range of input rows. Lane l of a
-//    warp reads columns [8l, 8l+8) of a row: each row of the tile is one 512-byte
-//    coalesced run, 16 bytes per lane (evict-first L2 policy: weights are streamed
-//    once per token). A warp takes blocks of 8 consecutive rows and keeps the next
-//    block's loads in flight while it multiplies the current one.
+//    256 columns of gate and up) and a contiguous range of input rows. A warp takes
+//    blocks of 8 consecutive rows of the tile (8 x 512 contiguous bytes per row) and
+//    streams them through its own 3-slot shared-memory ring with 2D TMA copies that
+//    its lane 0 issues (evict-first L2 policy: weights are streamed once per token);
+//    each slot is refilled as soon as the warp has multiplied it, and no warp waits
+//    for another. Lane l multiplies columns [8l, 8l+8) of every row (16-byte shared
+//    loads, fp32 fused multiply-adds in row order). Measured against an earlier
+//    version that kept two blocks of 16-byte global loads in registers per warp: the
+//    registers capped the bytes in flight per SM and the stream at about 81% of the
+//    copy bandwidth even in the longest launch.
 //  * The CTAs of one tile split its rows and form a thread-block cluster (up to 16
 //    CTAs). Each CTA sums its warps' partials through shared memory in warp order,
 //    then every CTA of the cluster sums one slice of the tile's columns over the
@@ -29,9 +34,12 @@
 //    rows; the sum of squares over the whole input costs one 8-24 KB read from L2.
 //  * Epilogue per column: T(sum); SwiGLU: T(silu(g) * u) from the rounded g and u, as
 //    the reference's swiglu kernel; residual: T(T(sum) + r), as its add kernel.
-//  * Programmatic dependent launch (QIC_PDL): the first block of weight rows is
-//    loaded before griddepcontrol.wait (weights are constants), the input, norm
-//    weights and residual after it.
+//  * Programmatic dependent launch (QIC_PDL): the ring's first fill is issued before
+//    griddepcontrol.wait (weights are constants), the input, norm weights and
+//    residual are read after it.
+//  * Every wait is bounded (ptx.cuh): on timeout the warp records QIC_DEV_TIMEOUT in
+//    the caller's status word (if any), drains its copies (bounded) and the CTA
+//    finishes without writing outputs.
 //
 // Compiled with --use_fast_math, like the reference build, so rsqrtf and expf in the
 // fused norm and SwiGLU are the same approximations.
@@ -45,17 +53,13 @@ namespace qic {
 namespace {
 
 constexpr int kWarps = kGemvThreads / 32;
-constexpr int kTile = kGemvTile;  // columns per tile
-constexpr int kU = 8;             // rows per block of a warp
+constexpr int kTile = kGemvTile;                         // columns per tile
+constexpr int kRowsSlot = kGemvRowsPerSlot;              // rows per TMA box (one ring slot)
+constexpr int kSlotsW = kGemvSlotsPerWarp;               // ring slots per warp
+constexpr int kSlotBytes = kRowsSlot * kTile * 2;        // 4 KB
+constexpr int kRingBytes = kWarps * kSlotsW * kSlotBytes;  // 96 KB
 constexpr int kRedRow = kTile + 4;
-
-__device__ __forceinline__ uint4 ld_weights(const void* p, uint64_t pol) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p), "l"(pol));
-  return v;
-}
+static_assert(kRingBytes >= (kWarps * kRedRow + 2 * kTile) * 4, "warp partials reuse the ring");
 
 template <typename T>
 __device__ __forceinline__ void fma8(float (&acc)[8], const uint4& w, float x) {
@@ -80,11 +84,15 @@ __device__ __forceinline__ X* map_rank(X* p, int rank) {
 // gate rows, warps 4-7 the same columns of up); out = silu(gate) * up into segment 0.
 template <typename T, bool PAIR, bool NORM>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
-  extern __shared__ __align__(16) float gsm[];
-  float* xs = gsm;                                   // [rows of this CTA] normalised input
-  float* red = gsm + p.xs_floats;                    // [kWarps][kRedRow] warp partials
-  float* part = red + kWarps * kRedRow;              // [2][kTile] this CTA's partial (gate, up)
+  extern __shared__ uint8_t gsm_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes);  // [kWarps][kSlotsW]
+  float* xs = reinterpret_cast<float*>(full + kWarps * kSlotsW);     // [rows of this CTA] input
+  // after the stream the ring is free: warp partials and the CTA's partial live there
+  float* red = reinterpret_cast<float*>(ring);                       // [kWarps][kRedRow]
+  float* part = red + kWarps * kRedRow;                              // [2][kTile] (gate, up)
   __shared__ float wsum[kWarps];
+  __shared__ int aborted;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C = p.splits;
@@ -100,35 +108,46 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int r0 = crank * p.rows_per_split;
   const int r1 = min(p.K, r0 + p.rows_per_split);
   const int nrows = max(0, r1 - r0);
+  const int nblk = (nrows + kRowsSlot - 1) / kRowsSlot;  // blocks of kRowsSlot rows in this CTA's range
 
-  // this warp's weights: its segment (gate or up for a pair), column block of the lane
+  // this warp's weights (gate or up for a pair) and its blocks: wslot, wslot + wstride, ...
   const int wseg = PAIR ? (warp >= kWarps / 2 ? 1 : 0) : s;
-  const int wslot = PAIR ? (warp & (kWarps / 2 - 1)) : warp;   // warp index within its group
-  const int wstride = PAIR ? kWarps / 2 : kWarps;              // warps sharing the rows
-  const int col = c0 + lane * 8;
-  const bool col_ok = col < N;
-  const T* wbase = static_cast<const T*>(p.seg[wseg].w) + static_cast<size_t>(r0) * N + col;
+  const int wslot = PAIR ? (warp & (kWarps / 2 - 1)) : warp;
+  const int wstride = PAIR ? kWarps / 2 : kWarps;
+  const int nmine = wslot < nblk ? (nblk - wslot + wstride - 1) / wstride : 0;
+  const CUtensorMap* tm = &p.tm[wseg];
+  uint8_t* wring = ring + warp * kSlotsW * kSlotBytes;
+  uint64_t* wfull = full + warp * kSlotsW;
   const uint64_t pol = l2_policy_evict_first();
-  const int nblk = (nrows + kU - 1) / kU;  // blocks of kU rows in this CTA's range
+  const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
 
+  if (lane == 0) {
+    if (warp == 0) aborted = 0;
+#pragma unroll
+    for (int k = 0; k < kSlotsW; ++k) mbar_init(&wfull[k], 1);
+    fence_mbar_init();
+    tma_prefetch_desc(tm);
+  }
+  __syncwarp();
   pdl_launch_gemv();
 
-  auto load_block = [&](uint4 (&v)[kU], int blk) {
-    const int rb = blk * kU;
-#pragma unroll
-    for (int j = 0; j < kU; ++j) {
-      const int r = rb + j;
-      if (col_ok && r < nrows)
-        v[j] = ld_weights(wbase + static_cast<size_t>(r) * N, pol);
-      else
-        v[j] = make_uint4(0u, 0u, 0u, 0u);
+  // Block m of this warp: rows r0 + (wslot + m*wstride)*kRowsSlot .. +kRowsSlot, all
+  // kTile columns of the tile, one 2D TMA box into ring slot m % kSlotsW. Rows past
+  // the input's end are filled with zeros by the copy.
+  auto issue = [&](int m) {
+    if (lane == 0) {
+      const int k = m % kSlotsW;
+      mbar_arrive_expect_tx(&wfull[k], kSlotBytes);
+      tma_load_2d(wring + k * kSlotBytes, tm, &wfull[k], c0, r0 + (wslot + m * wstride) * kRowsSlot, pol);
     }
   };
-
-  // first block of weights before the preceding kernel's outputs are waited for
-  uint4 bufA[kU], bufB[kU];
-  int blk = wslot;
-  if (blk < nblk) load_block(bufA, blk);
+  // the ring's first fill before the preceding kernel's outputs are waited for
+  // (weights are constants). Measured and not kept: also prefetching the warp's next
+  // 4 / 16 / 64 blocks into L2 here (Qwen3-8B projection chain 19.6 -> 19.7 / 21.0 /
+  // 22.0 us per launch).
+#pragma unroll
+  for (int m = 0; m < kSlotsW; ++m)
+    if (m < nmine) issue(m);
   if (p.flags & QIC_PDL) pdl_wait_gemv();
 
   // ---- the input of this CTA's rows, normalised when NORM ----
@@ -154,7 +173,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   {
     const T* x = static_cast<const T*>(p.x) + r0;
     const T* nw = NORM ? static_cast<const T*>(p.norm_w) + r0 : nullptr;
-    for (int i = threadIdx.x; i < nblk * kU; i += kGemvThreads) {
+    for (int i = threadIdx.x; i < nblk * kRowsSlot; i += kGemvThreads) {
       float v = 0.0f;
       if (i < nrows) {
         v = to_f32<T>(x[i]);
@@ -165,33 +184,49 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   }
   __syncthreads();
 
-  // ---- stream the rows: block blk in one buffer while the next one loads ----
+  // ---- stream: wait for a slot, multiply its rows, refill it ----
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-  auto fma_block = [&](const uint4 (&v)[kU], int b) {
-    const float4 xa = *reinterpret_cast<const float4*>(xs + b * kU);
-    const float4 xb = *reinterpret_cast<const float4*>(xs + b * kU + 4);
-    fma8<T>(acc, v[0], xa.x);
-    fma8<T>(acc, v[1], xa.y);
-    fma8<T>(acc, v[2], xa.z);
-    fma8<T>(acc, v[3], xa.w);
-    fma8<T>(acc, v[4], xb.x);
-    fma8<T>(acc, v[5], xb.y);
-    fma8<T>(acc, v[6], xb.z);
-    fma8<T>(acc, v[7], xb.w);
-  };
+  bool ok = true;
+  int m = 0;
 #pragma unroll 1
-  while (blk < nblk) {
-    const int nb = blk + wstride;
-    if (nb < nblk) load_block(bufB, nb);
-    fma_block(bufA, blk);
-    if (nb >= nblk) break;
-    const int nb2 = nb + wstride;
-    if (nb2 < nblk) load_block(bufA, nb2);
-    fma_block(bufB, nb);
-    blk = nb2;
+  for (; m < nmine; ++m) {
+    const int k = m % kSlotsW;
+    if (!__all_sync(kFullMask, mbar_wait(&wfull[k], (m / kSlotsW) & 1, deadline))) {
+      ok = false;
+      break;
+    }
+    const uint8_t* slot = wring + k * kSlotBytes + lane * 16;
+    const float* xb = xs + (wslot + m * wstride) * kRowsSlot;
+    const float4 xa = *reinterpret_cast<const float4*>(xb);
+    const float4 xc = *reinterpret_cast<const float4*>(xb + 4);
+    const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+    for (int j = 0; j < kRowsSlot; ++j) {
+      const uint4 w = *reinterpret_cast<const uint4*>(slot + j * (kTile * 2));
+      fma8<T>(acc, w, xr[j]);
+    }
+    // the slot's values are consumed (the accumulators depend on every row) before
+    // the copy that overwrites it is issued
+    asm volatile("" ::"f"(acc[0]), "f"(acc[1]), "f"(acc[2]), "f"(acc[3]), "f"(acc[4]), "f"(acc[5]), "f"(acc[6]),
+                 "f"(acc[7])
+                 : "memory");
+    __syncwarp();
+    if (m + kSlotsW < nmine) issue(m + kSlotsW);
   }
+  if (!ok) {
+    if (lane == 0) {
+      record_status(p.status, QIC_DEV_TIMEOUT);
+      aborted = 1;
+    }
+    // wait (bounded) for this warp's copies still in flight before the ring is reused
+    const uint64_t dl2 = globaltimer_ns() + p.timeout_ns;
+    for (int mm = m; mm < nmine && mm < m + kSlotsW; ++mm)
+      mbar_wait(&wfull[mm % kSlotsW], (mm / kSlotsW) & 1, dl2);
+    __syncwarp();
+  }
+  __syncthreads();  // every warp is past its stream: the ring holds no copy in flight
 
   // ---- the CTA's partial: warps summed in order ----
   {
@@ -230,14 +265,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int t = lo + threadIdx.x;
   if (t < hi) {
     float g = 0.0f, u = 0.0f;
+    int bad = 0;  // a CTA of the cluster gave up on a copy: its partial is incomplete
     if (C > 1) {
       float pg[kGemvMaxSplits], pu[kGemvMaxSplits];
+      int pb[kGemvMaxSplits];
 #pragma unroll
       for (int c = 0; c < kGemvMaxSplits; ++c) {
         if (c < C) {
           const float* rp = map_rank(part, c);
           pg[c] = rp[t];
           pu[c] = PAIR ? rp[kTile + t] : 0.0f;
+          pb[c] = *map_rank(&aborted, c);
         }
       }
 #pragma unroll
@@ -245,14 +283,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         if (c < C) {
           g += pg[c];
           u += pu[c];
+          bad |= pb[c];
         }
       }
     } else {
       g = part[t];
       u = PAIR ? part[kTile + t] : 0.0f;
+      bad = aborted;
     }
     const int oc = c0 + t;
-    if (oc < N) {
+    if (oc < N && !bad) {
       T* out = static_cast<T*>(p.seg[s].out);
       if (PAIR) {
         const float gv = to_f32<T>(from_f32<T>(g));
@@ -335,8 +375,8 @@ int max_clusters_typed(int cluster, size_t smem) {
 }  // namespace
 
 size_t gemv_smem_bytes(int rows_per_split) {
-  const int xs = ((rows_per_split + kU - 1) / kU) * kU;
-  return static_cast<size_t>(xs + kWarps * kRedRow + 2 * kTile) * sizeof(float);
+  const int xs = ((rows_per_split + kRowsSlot - 1) / kRowsSlot) * kRowsSlot;
+  return 1024 + kRingBytes + kWarps * kSlotsW * sizeof(uint64_t) + static_cast<size_t>(xs) * sizeof(float);
 }
 
 int gemv_max_active_clusters(int dtype, int cluster, int rows_per_split) {

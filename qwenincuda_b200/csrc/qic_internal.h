@@ -115,6 +115,8 @@ constexpr int kGemvTile = 256;
 constexpr int kGemvMaxSegments = QIC_GEMV_MAX_SEGMENTS;
 constexpr int kGemvMaxSplits = 16;
 constexpr int kGemvMaxRowsPerSplit = 8192;  // normalised input rows kept in shared memory
+constexpr int kGemvRowsPerSlot = 8;         // rows per TMA box / ring slot (8 x 512 B)
+constexpr int kGemvSlotsPerWarp = 3;        // ring slots per warp
 
 struct GemvSeg {
   const void* w;    // [K, N], N contiguous
@@ -125,6 +127,7 @@ struct GemvSeg {
 };
 
 struct GemvParams {
+  CUtensorMap tm[kGemvMaxSegments];  // 2D map of each segment's weights {N, K}, box {kGemvTile, kGemvRowsPerSlot}
   const void* x;       // [K]
   const void* norm_w;  // [K] or null
   float eps;
@@ -135,6 +138,8 @@ struct GemvParams {
   int splits;          // CTAs per cluster along the rows
   int rows_per_split;
   int xs_floats;       // floats of the input slice in shared memory (rows_per_split rounded up to 8)
+  int* status;         // device status word (QIC_DEV_TIMEOUT) or null
+  uint64_t timeout_ns;
   GemvSeg seg[kGemvMaxSegments];
 };
 

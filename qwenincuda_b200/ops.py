@@ -293,7 +293,7 @@ def batch_decode_attention(stream=None, **kw):
 
 
 def gemv_args(*, x, weights, outs, residuals=None, norm_w=None, eps=1e-6, swiglu=False, pdl=False,
-              splits=0) -> "GemvArgs":
+              splits=0, status=None) -> "GemvArgs":
     """qic_gemv_args for one launch: x [K]; weights: list of [K, N_k] tensors (N_k
     contiguous, the reference's column-major layout); outs: list of [N_k] outputs (with
     swiglu, weights = [w_gate, w_up] and outs = [out], silu(gate)*up); residuals: list
@@ -327,6 +327,10 @@ def gemv_args(*, x, weights, outs, residuals=None, norm_w=None, eps=1e-6, swiglu
         a.seg[k].out = _ptr(outs[k])
         if residuals is not None:
             a.seg[k].residual = _ptr(residuals[k])
+    if status is not None:
+        if status.dtype != torch.int32 or not status.is_cuda:
+            raise TypeError("status is a CUDA int32 tensor")
+        a.status = status.data_ptr()
     a.flags = flags
     return a
 

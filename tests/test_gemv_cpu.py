@@ -26,8 +26,8 @@ def _call(a):
 
 
 def test_layout():
-    # 4 int32 + 2 pointers + float + int32 + 4 segments of (3 pointers + 2 int32)
-    assert ctypes.sizeof(GemvArgs) == 16 + 16 + 8 + 4 * 32
+    # 4 int32 + 2 pointers + float + int32 + 4 segments of (3 pointers + 2 int32) + status pointer
+    assert ctypes.sizeof(GemvArgs) == 16 + 16 + 8 + 4 * 32 + 8
 
 
 @pytest.mark.parametrize("mutate,status", [

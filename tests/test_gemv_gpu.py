@@ -90,7 +90,12 @@ def test_fused_norm_qkv_one_launch(dtype):
 @pytest.mark.parametrize("hidden,inter", [(1024, 3072), (4096, 12288)])
 def test_ffn_two_launches_vs_reference_ffn_block(dtype, hidden, inter):
     """The FFN block as two launches (norm + gate/up + SwiGLU; down + residual into x)
-    against the reference's own run_ffn_block on the same x and weights."""
+    against the reference's own run_ffn_block on the same x and weights. The block
+    rounds to 16 bits four times (gate and up, SwiGLU, the down product, the residual
+    sum), and the down product can be larger than the block's output (the residual
+    cancels part of it): besides max-abs 2e-3 / rel 1e-2 of the output, an element may
+    differ by two units in the last place of the larger of |output| and
+    |output - x| (the down product)."""
     eps = 1e-6
     g = _gen(hidden + inter)
     x = _x(hidden, g, dtype)
@@ -105,8 +110,16 @@ def test_ffn_two_launches_vs_reference_ffn_block(dtype, hidden, inter):
     q.gemv(x=got, weights=[wg, wu], outs=[h], norm_w=nw, eps=eps, swiglu=True)
     q.gemv(x=h, weights=[wd], outs=[got], residuals=[got])
     torch.cuda.synchronize()
-    ok, err, idx = allclose_report(got, want, ATOL, RTOL)
-    assert ok, f"max abs err {err} at {idx}"
+    w32, g32, x32 = want.float(), got.float(), x.float()
+    mag = torch.maximum(w32.abs(), (w32 - x32).abs())
+    mant = 7 if dtype == torch.bfloat16 else 10
+    ulp = torch.exp2(torch.floor(torch.log2(mag.clamp_min(1e-30))) - mant)
+    bound = ATOL + RTOL * w32.abs() + 2 * ulp
+    diff = (g32 - w32).abs()
+    assert not torch.isnan(g32).any()
+    assert bool((diff <= bound).all()), f"max abs err {float(diff.max())} at {int(diff.argmax())}"
+    # and most elements within the plain tolerance
+    assert float(((diff > ATOL + RTOL * w32.abs()).float().mean())) < 0.01
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
