@@ -77,8 +77,10 @@ def load_peaks():
 
 def measured_traffic(workload: str):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary of
-    this workload (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch: N')."""
-    for p in (ROOT / "profiles").glob(f"*_{workload}.md"):
+    this workload (profiles/<kernel>_<workload>.md or profiles/<workload>.md, line
+    'traffic_bytes_per_launch: N')."""
+    paths = list((ROOT / "profiles").glob(f"*_{workload}.md")) + list((ROOT / "profiles").glob(f"{workload}.md"))
+    for p in paths:
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
                 try:
@@ -899,7 +901,7 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def summarize(wl, ms, ms_e2e, peaks, kernel_ms=None):
+def summarize(wl, ms, ms_e2e, peaks, kernel_ms=None, workload=None):
     """One workload's figures on one GPU: GB/s, us per layer, the roofline fraction of
     its dominant kernel, and the end-to-end figure."""
     per_launch_ms = ms / wl["launches"]
@@ -908,7 +910,8 @@ def summarize(wl, ms, ms_e2e, peaks, kernel_ms=None):
             "us_per_layer": round(per_launch_ms * 1000, 3),
             "roofline": {"bound": "hbm", "kernel": wl["kernel"], "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"]},
+                         "frac_of_8tbs": round(achieved / 8000.0, 4), "bytes_per_launch": wl["bytes_per_launch"],
+                         "traffic": measured_traffic(workload) if workload else None},
             "e2e": {"value": round(wl["bytes"] / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": wl["e2e"][1], "d2h_bytes_per_step": wl["e2e"][2]},
             "config": wl["config"]}
@@ -1053,18 +1056,18 @@ def main():
             for name in ("qwen35_gated_s32769", "qwen3_0p6b_s1025"):
                 w2 = attention_workload(name, "paged")
                 m2, e2, _ = measure(w2, args, 1, local)
-                extra[name] = summarize(w2, m2, e2, peaks)
+                extra[name] = summarize(w2, m2, e2, peaks, workload=name)
                 del w2
                 torch.cuda.empty_cache()
             w2 = gdn_workload()
             m2, e2, _ = measure(w2, args, 1, local)
-            extra["qwen35_gdn"] = summarize(w2, m2, e2, peaks)
+            extra["qwen35_gdn"] = summarize(w2, m2, e2, peaks, workload="qwen35_gdn")
             del w2
             torch.cuda.empty_cache()
             # the projections around the attention of the same model (weight bytes)
             w2 = gemv_workload()
             m2, e2, _ = measure(w2, args, 1, local)
-            extra["gemv_qwen3_8b"] = summarize(w2, m2, e2, peaks)
+            extra["gemv_qwen3_8b"] = summarize(w2, m2, e2, peaks, workload="gemv_qwen3_8b")
             extra["gemv_qwen3_8b"]["us_per_model_layer"] = round(m2 * 1000 / w2["config"]["layers"], 2)
             gl = capture(w2["library_step"])
             ml = time_graph(gl, args.steps, args.warmup, 1)
