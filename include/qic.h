@@ -422,6 +422,80 @@ typedef struct qic_gdn_args {
  * read-out, gated RMSNorm. */
 int qic_gated_delta_decode(const qic_gdn_args* args, qic_stream_t stream);
 
+/* ------------------------------------------------------------------------- */
+/* Decode-step runner: decode_next as one captured CUDA graph.                 */
+/* ------------------------------------------------------------------------- */
+
+/* The model's shape: the fields of QwenMiniConfig (include/model.hpp:10-28), in the
+ * order of the qmini v4 header (src/model.cpp:345-366). layer_types[i]: 0 full
+ * attention, 1 linear attention (GatedDeltaNet). */
+typedef struct qic_model_config {
+  int32_t vocab_size, hidden_size, intermediate_size, num_layers;
+  int32_t num_heads, num_kv_heads, head_dim;
+  int32_t linear_num_key_heads, linear_num_value_heads, linear_key_head_dim, linear_value_head_dim;
+  int32_t linear_conv_kernel_dim;
+  int32_t max_seq_len;
+  float rms_norm_eps, rope_theta;
+  const int32_t* layer_types;  /* [num_layers] */
+} qic_model_config;
+
+/* Device weights of one layer: QwenMiniModel::LayerWeights (include/model.hpp:55-79),
+ * the same shapes and column-major [in][out] projection layout. */
+typedef struct qic_layer_weights {
+  int32_t is_linear;
+  const void* attn_norm;
+  const void *wq, *wk, *wv, *q_norm, *k_norm, *wo;  /* full attention (wq: [hidden, 2*H*d], q and gate) */
+  const void *linear_in_qkv, *linear_in_z, *linear_in_b, *linear_in_a, *linear_conv1d_w, *linear_dt_bias,
+      *linear_a_log, *linear_norm_w, *linear_out_proj;  /* linear attention */
+  const void *ffn_norm, *w_gate, *w_up, *w_down;
+} qic_layer_weights;
+
+typedef struct qic_model_weights {
+  const void* tok_embeddings;        /* [vocab, hidden] */
+  const void* final_norm;            /* [hidden] */
+  const void* lm_head;               /* [hidden, vocab] */
+  const qic_layer_weights* layers;   /* [num_layers] */
+} qic_model_weights;
+
+typedef struct qic_model qic_model;
+
+/* A runner over the caller's device weights (they must outlive it). Allocates the
+ * K/V caches ([max_seq_len, kv_dim] per full-attention layer), the fp32 conv and
+ * recurrent states, the runtime buffers and the attention workspace, runs one step,
+ * captures the step as a CUDA graph and clears the caches and states. No counterpart
+ * function in the reference: its QwenMiniModel is set up by load() (src/model.cpp:
+ * 319-428) and alloc_runtime() (src/model.cpp:430-502). */
+int qic_model_create(const qic_model_config* cfg, int dtype, const qic_model_weights* weights, qic_model** model);
+
+/* A runner over the weights of a qmini v4 file (QwenMiniModel::load, src/model.cpp:
+ * 319-428: the same header checks and tensor order), kept as 16-bit values on the
+ * device (QIC_DTYPE_F16). max_seq_len 0 keeps the file's. */
+int qic_model_load(const char* path, int max_seq_len, qic_model** model);
+
+/* The runner's shape (layer_types not returned) and its file weight bytes (0 for qic_model_create). */
+int qic_model_info(const qic_model* model, qic_model_config* cfg, size_t* weight_bytes);
+
+/* Clears the K/V caches, the linear-attention states and the device status words (a new sequence). */
+int qic_model_reset(qic_model* model);
+
+/* One decode step at `position` (0-based; the caches hold positions 0..position-1):
+ * QwenMiniModel::decode_next (src/model.cpp:823-845). Copies the token and length to
+ * the device, replays the step's graph on `stream`, and returns the greedy token
+ * (argmax_host, src/model.cpp:78-89: first index of the largest logit) in
+ * *next_token and, when logits is not NULL, the vocab_size 16-bit logits (host
+ * memory). Synchronises `stream`. QIC_ERROR_DEVICE_TIMEOUT / QIC_ERROR_BAD_PAGE report
+ * a device-side status bit of this step. */
+int qic_model_decode(qic_model* model, int token, int position, void* logits, int* next_token, qic_stream_t stream);
+
+/* The two halves of qic_model_decode without the synchronisation, for callers that
+ * time or chain steps: write the token and position (stream-ordered), then replay the
+ * step's graph. The greedy token stays on the device. */
+int qic_model_set_position(qic_model* model, int token, int position, qic_stream_t stream);
+int qic_model_step_graph(qic_model* model, qic_stream_t stream);
+
+/* Frees the runner (and the weights qic_model_load read); synchronises the device. */
+int qic_model_free(qic_model* model);
+
 #ifdef __cplusplus
 }
 #endif

@@ -320,6 +320,39 @@ class RefModel:
             raise RuntimeError("reference FFN block failed")
 
 
+class RefQwenModel:
+    """The reference model end to end: QwenMiniModel::load of a qmini v4 file and
+    decode_next (src/model.cpp:319-428, 823-845), compiled unchanged into
+    oracle/_ref/libqicref_gdn.so (fp16, as the format stores)."""
+
+    def __init__(self, path):
+        lib_path = REF_DIR / "libqicref_gdn.so"
+        if not lib_path.exists():
+            raise FileNotFoundError(f"{lib_path} not built (make -C oracle ref REF=<reference project root>)")
+        lib = ctypes.CDLL(str(lib_path), mode=ctypes.RTLD_LOCAL)
+        lib.qicref_model_load.argtypes = [ctypes.c_char_p]
+        lib.qicref_model_load.restype = _vp
+        lib.qicref_model_decode.argtypes = [_vp, _i, _i, _vp]
+        lib.qicref_model_decode.restype = _i
+        lib.qicref_model_free.argtypes = [_vp]
+        self.lib = lib
+        self.h = lib.qicref_model_load(str(path).encode())
+        if not self.h:
+            raise RuntimeError(f"reference load of {path} failed")
+
+    def decode(self, token, position, logits=None):
+        """decode_next(token, position): the greedy token; `logits` (CPU fp16, vocab) receives the logits."""
+        nxt = self.lib.qicref_model_decode(self.h, int(token), int(position), _p(logits))
+        if nxt < 0:
+            raise RuntimeError("reference decode_next failed")
+        return nxt
+
+    def close(self):
+        if self.h:
+            self.lib.qicref_model_free(self.h)
+            self.h = None
+
+
 class _RefGatedDeltaLayer:
     def __init__(self, lib, dtype, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, Hk, Hv, dk, dv, K,
                  eps):

@@ -257,3 +257,39 @@ extern "C" int qicref_ffn_block(void* x, const void* ffn_norm, const void* w_gat
   }
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// The reference model end to end: QwenMiniModel::load of a qmini v4 file
+// (src/model.cpp:319-428) and decode_next (src/model.cpp:823-845), unmodified.
+// ---------------------------------------------------------------------------
+extern "C" void* qicref_model_load(const char* path) {
+  QwenMiniModel* m = new QwenMiniModel();
+  try {
+    if (!m->load(path)) {
+      delete m;
+      return nullptr;
+    }
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "reference load failed: %s\n", e.what());
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+
+// One decode_next step; logits (host, vocab 16-bit values) may be null. Returns the
+// greedy token, or -1 after printing the reference's error.
+extern "C" int qicref_model_decode(void* handle, int token, int position, void* logits) {
+  QwenMiniModel* m = static_cast<QwenMiniModel*>(handle);
+  try {
+    std::vector<half> host;
+    const int next = m->decode_next(token, position, &host);
+    if (logits != nullptr) std::memcpy(logits, host.data(), host.size() * sizeof(half));
+    return next;
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "reference decode_next failed: %s\n", e.what());
+    return -1;
+  }
+}
+
+extern "C" void qicref_model_free(void* handle) { delete static_cast<QwenMiniModel*>(handle); }

@@ -197,6 +197,35 @@ class GemvArgs(ctypes.Structure):
     ]
 
 
+class ModelConfig(ctypes.Structure):
+    """Mirror of qic_model_config."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "vocab_size", "hidden_size", "intermediate_size", "num_layers", "num_heads", "num_kv_heads", "head_dim",
+        "linear_num_key_heads", "linear_num_value_heads", "linear_key_head_dim", "linear_value_head_dim",
+        "linear_conv_kernel_dim", "max_seq_len")] + [
+        ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+        ("layer_types", ctypes.POINTER(ctypes.c_int32))]
+
+
+LAYER_WEIGHT_NAMES = ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "linear_in_qkv", "linear_in_z",
+                      "linear_in_b", "linear_in_a", "linear_conv1d_w", "linear_dt_bias", "linear_a_log",
+                      "linear_norm_w", "linear_out_proj", "ffn_norm", "w_gate", "w_up", "w_down")
+
+
+class LayerWeights(ctypes.Structure):
+    """Mirror of qic_layer_weights."""
+
+    _fields_ = [("is_linear", ctypes.c_int32)] + [(n, ctypes.c_void_p) for n in LAYER_WEIGHT_NAMES]
+
+
+class ModelWeights(ctypes.Structure):
+    """Mirror of qic_model_weights."""
+
+    _fields_ = [("tok_embeddings", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("lm_head", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(LayerWeights))]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -223,6 +252,15 @@ SIGNATURES = {
                                                ctypes.POINTER(ctypes.c_int)]),
     "qic_gated_delta_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), _vp]),
     "qic_gemv": (ctypes.c_int, [ctypes.POINTER(GemvArgs), _vp]),
+    "qic_model_create": (ctypes.c_int, [ctypes.POINTER(ModelConfig), ctypes.c_int, ctypes.POINTER(ModelWeights),
+                                        ctypes.POINTER(ctypes.c_void_p)]),
+    "qic_model_load": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "qic_model_info": (ctypes.c_int, [_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(ctypes.c_size_t)]),
+    "qic_model_reset": (ctypes.c_int, [_vp]),
+    "qic_model_decode": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.POINTER(ctypes.c_int), _vp]),
+    "qic_model_set_position": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "qic_model_step_graph": (ctypes.c_int, [_vp, _vp]),
+    "qic_model_free": (ctypes.c_int, [_vp]),
     "qic_gemv_launch_shape": (ctypes.c_int, [ctypes.POINTER(GemvArgs), ctypes.POINTER(ctypes.c_int),
                                              ctypes.POINTER(ctypes.c_int)]),
     "qic_batch_plan": (

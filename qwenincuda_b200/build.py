@@ -34,6 +34,8 @@ UNITS = [
     ("compat.cu", ["--use_fast_math"]),
     ("noalloc.cu", []),
     ("gemv_kernel.cu", ["--use_fast_math"]),
+    ("runtime_kernels.cu", []),
+    ("model_runner.cpp", []),
 ]
 
 

@@ -347,3 +347,68 @@ def gemv_launch_shape(**kw) -> tuple[int, int]:
     s, t = ctypes.c_int(0), ctypes.c_int(0)
     check(lib().qic_gemv_launch_shape(ctypes.byref(a), ctypes.byref(s), ctypes.byref(t)), "qic_gemv_launch_shape")
     return s.value, t.value
+
+
+class Model:
+    """A decode-step runner (qic_model_*): load(path) for a qmini v4 file, or
+    from_weights(config, dtype, weights) over device tensors the caller keeps alive.
+    decode(token, position) replays the captured step and returns the greedy token
+    (and the logits when asked), like the reference's QwenMiniModel::decode_next."""
+
+    def __init__(self, handle: int, keep=None):
+        self.handle = ctypes.c_void_p(handle)
+        self._keep = keep
+        cfg = __import__("qwenincuda_b200.abi", fromlist=["ModelConfig"]).ModelConfig()
+        wb = ctypes.c_size_t(0)
+        check(lib().qic_model_info(self.handle, ctypes.byref(cfg), ctypes.byref(wb)), "qic_model_info")
+        self.config = cfg
+        self.weight_bytes = wb.value
+
+    @classmethod
+    def load(cls, path, max_seq_len: int = 0) -> "Model":
+        h = ctypes.c_void_p(0)
+        check(lib().qic_model_load(str(path).encode(), max_seq_len, ctypes.byref(h)), "qic_model_load")
+        return cls(h.value)
+
+    @classmethod
+    def from_weights(cls, config, dtype: int, tok_embeddings, final_norm, lm_head, layers) -> "Model":
+        """layers: list of dicts of tensors keyed by qic_layer_weights field names (plus is_linear)."""
+        from .abi import LayerWeights, ModelConfig, ModelWeights
+
+        arr = (LayerWeights * len(layers))()
+        for i, lw in enumerate(layers):
+            arr[i].is_linear = int(lw.get("is_linear", 0))
+            for k, t in lw.items():
+                if k != "is_linear" and t is not None:
+                    setattr(arr[i], k, t.data_ptr())
+        types = (ctypes.c_int32 * len(layers))(*[int(lw.get("is_linear", 0)) for lw in layers])
+        cfg = ModelConfig(**{k: v for k, v in config.items() if k != "layer_types"})
+        cfg.layer_types = ctypes.cast(types, ctypes.POINTER(ctypes.c_int32))
+        w = ModelWeights(tok_embeddings=tok_embeddings.data_ptr(), final_norm=final_norm.data_ptr(),
+                         lm_head=lm_head.data_ptr(), layers=ctypes.cast(arr, ctypes.POINTER(LayerWeights)))
+        h = ctypes.c_void_p(0)
+        check(lib().qic_model_create(ctypes.byref(cfg), dtype, ctypes.byref(w), ctypes.byref(h)), "qic_model_create")
+        return cls(h.value, keep=(tok_embeddings, final_norm, lm_head, layers))
+
+    def reset(self) -> None:
+        check(lib().qic_model_reset(self.handle), "qic_model_reset")
+
+    def decode(self, token: int, position: int, logits=None, stream=None) -> int:
+        """Greedy next token; `logits`: optional CPU 16-bit tensor of vocab_size elements."""
+        nxt = ctypes.c_int(-1)
+        ptr = None if logits is None else ctypes.c_void_p(logits.data_ptr())
+        check(lib().qic_model_decode(self.handle, int(token), int(position), ptr, ctypes.byref(nxt), _stream(stream)),
+              "qic_model_decode")
+        return nxt.value
+
+    def set_position(self, token: int, position: int, stream=None) -> None:
+        check(lib().qic_model_set_position(self.handle, int(token), int(position), _stream(stream)),
+              "qic_model_set_position")
+
+    def step_graph(self, stream=None) -> None:
+        check(lib().qic_model_step_graph(self.handle, _stream(stream)), "qic_model_step_graph")
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().qic_model_free(self.handle), "qic_model_free")
+            self.handle = ctypes.c_void_p(0)

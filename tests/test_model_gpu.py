@@ -1,0 +1,128 @@
+"""GPU: whole decode steps on a synthetic Qwen3.5-style model (three GatedDeltaNet
+layers and one gated full-attention layer, fp16, seeded weights written in the
+reference's qmini v4 format by oracle/qmini_writer.py).
+
+* The runner (qic_model_load / qic_model_decode: decode_next as one CUDA graph of this
+  library's kernels) against the reference model itself (QwenMiniModel::load and
+  decode_next, src/model.cpp:319-428, 823-845, compiled unchanged into oracle/_ref):
+  a 140-token prompt (past the reference's switch from flash to paged attention at 128
+  tokens, src/model.cpp:644) and 24 greedy steps, the reference's token fed to both.
+  Every step's logits within max-abs 3e-2 / rel 2e-2 (four layers of 16-bit rounding
+  in two different accumulation orders, and a recurrent state carried over 164
+  tokens), and the same greedy token wherever the reference's best logit leads the
+  second by more than that.
+* The drop-in: the reference's own src/main.cpp and src/model.cpp, unmodified, linked
+  against libqic.so instead of src/kernels.cu (oracle/_ref/qwen_minimal_qic), against
+  the reference's own build of the same sources (oracle/_ref/qwen_minimal_ref): the
+  same generated ids from the same prompt with greedy decoding, and every step's
+  top-5 logits within the same tolerance.
+"""
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import qwenincuda_b200 as q
+from oracle.oracle import REF_DIR, RefQwenModel
+from oracle.qmini_writer import QminiConfig, write_qmini
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 3e-2, 2e-2
+PROMPT = 140
+STEPS = 24
+
+
+@pytest.fixture(scope="module")
+def synth(tmp_path_factory):
+    path = tmp_path_factory.mktemp("qmini") / "synth_qwen35.qmini"
+    cfg = QminiConfig()
+    write_qmini(path, cfg, seed=11)
+    return path, cfg
+
+
+def _prompt(cfg, n, seed=5):
+    return np.random.default_rng(seed).integers(0, cfg.vocab_size, n).tolist()
+
+
+def _close(a, b):
+    a, b = a.float(), b.float()
+    diff = (a - b).abs()
+    return bool((diff <= ATOL + RTOL * b.abs()).all()) and not bool(torch.isnan(a).any()), float(diff.max())
+
+
+def test_runner_matches_reference_decode_next(synth):
+    path, cfg = synth
+    ref = RefQwenModel(path)
+    ours = q.ops.Model.load(path)
+    try:
+        assert ours.config.vocab_size == cfg.vocab_size and ours.config.num_layers == cfg.num_layers
+        lr = torch.empty(cfg.vocab_size, dtype=torch.float16)
+        lo = torch.empty(cfg.vocab_size, dtype=torch.float16)
+        tokens = _prompt(cfg, PROMPT)
+        worst = 0.0
+        for pos in range(PROMPT + STEPS):
+            tok = tokens[pos]
+            want = ref.decode(tok, pos, lr)
+            got = ours.decode(tok, pos, lo)
+            ok, err = _close(lo, lr)
+            worst = max(worst, err)
+            assert ok, f"position {pos}: logits differ, max abs {err}"
+            top2 = torch.topk(lr.float(), 2).values
+            if float(top2[0] - top2[1]) > ATOL + RTOL * float(top2[0].abs()):
+                assert got == want, f"position {pos}: greedy token {got} vs the reference's {want}"
+            if pos + 1 >= len(tokens):
+                tokens.append(want)
+        # a new sequence after reset gives the first step's logits again
+        ours.reset()
+        ours.decode(tokens[0], 0, lo)
+        ref2 = RefQwenModel(path)
+        try:
+            ref2.decode(tokens[0], 0, lr)
+        finally:
+            ref2.close()
+        assert _close(lo, lr)[0]
+    finally:
+        ours.close()
+        ref.close()
+
+
+def _run(exe, path, ids, steps):
+    out = subprocess.run([str(exe), "--model", str(path), "--input-ids", ",".join(map(str, ids)),
+                          "--max-new-tokens", str(steps), "--greedy-after", "0", "--dump-topk", "5",
+                          "--eos-id", "-1"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    gen = [int(t) for t in re.search(r"generated_ids=([0-9,]+)", out.stdout).group(1).split(",")]
+    tops = []
+    for line in out.stdout.splitlines():
+        m = re.match(r"step_topk\[(\d+)\]=(.*)", line)
+        if m:
+            tops.append([(int(a), float(b)) for a, b in (kv.split(":") for kv in m.group(2).split(","))])
+    return gen, tops
+
+
+def test_dropin_executable_matches_reference_executable(synth):
+    path, cfg = synth
+    exe_ref, exe_qic = REF_DIR / "qwen_minimal_ref", REF_DIR / "qwen_minimal_qic"
+    if not exe_ref.exists() or not exe_qic.exists():
+        pytest.fail("oracle/_ref executables not built (make -C oracle ref REF=<reference project root>)")
+    ids = _prompt(cfg, PROMPT, seed=6)
+    gen_ref, top_ref = _run(exe_ref, path, ids, STEPS)
+    gen_qic, top_qic = _run(exe_qic, path, ids, STEPS)
+    assert len(top_ref) == len(top_qic) == STEPS
+    assert gen_ref[:PROMPT] == gen_qic[:PROMPT] == ids
+    for step, (a, b) in enumerate(zip(top_ref, top_qic)):
+        va = {i: v for i, v in a}
+        for i, v in b:
+            if i in va:
+                assert abs(v - va[i]) <= ATOL + RTOL * abs(va[i]), f"step {step}, token {i}: {v} vs {va[i]}"
+        if gen_qic[PROMPT + step] != gen_ref[PROMPT + step]:
+            # only a near tie may resolve differently; after it the sequences differ
+            lead = a[0][1] - a[1][1]
+            assert lead <= ATOL + RTOL * abs(a[0][1]), (
+                f"step {step}: the drop-in chose {gen_qic[PROMPT + step]}, the reference "
+                f"{gen_ref[PROMPT + step]} (reference lead {lead:.4f})")
+            return
+    assert gen_qic == gen_ref
