@@ -568,6 +568,107 @@ def gemv_workload(layers=4, hidden=4096, inter=12288, q_out=4096, kv_out=1024, s
                         "what": "RMSNorm+q/k/v, o+residual, RMSNorm+gate/up+SwiGLU, down+residual"})
 
 
+QWEN35_4B = dict(vocab_size=151936, hidden_size=2560, intermediate_size=9216, num_heads=16, num_kv_heads=4,
+                 head_dim=256, linear_num_key_heads=16, linear_num_value_heads=32, linear_key_head_dim=128,
+                 linear_value_head_dim=128, linear_conv_kernel_dim=4, rms_norm_eps=1e-6, rope_theta=1.0e7)
+
+
+def decode_step_workload(context=4096, layer_types=(1, 1, 1, 0) * 8, seed=9):
+    """One whole decode step of a Qwen3.5-4B-shaped hybrid model (32 layers: 24
+    GatedDeltaNet, 8 gated full attention with 16/4 heads of 256; hidden 2560, FFN 9216,
+    vocab 151936) with random bf16 weights, through the decode-step runner
+    (qic_model_create + the captured step graph) at position `context` (the caches hold
+    `context` tokens). Bytes = weights + the K/V read by the attention layers + the
+    GatedDeltaNet states read and written."""
+    import qwenincuda_b200 as q
+    from qwenincuda_b200.abi import QIC_DTYPE_BF16
+    from qwenincuda_b200.workloads import GdnConfig
+
+    c = dict(QWEN35_4B, max_seq_len=context + 1, num_layers=len(layer_types))
+    dt = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    hid, inter, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
+    qd, kvd = c["num_heads"] * c["head_dim"], c["num_kv_heads"] * c["head_dim"]
+    kd, vd = c["linear_num_key_heads"] * 128, c["linear_num_value_heads"] * 128
+    conv, Hv = 2 * kd + vd, c["linear_num_value_heads"]
+
+    def w(*shape, std=None):
+        std = std if std is not None else 1.0 / shape[0] ** 0.5
+        return (torch.randn(*shape, generator=g, device="cuda") * std).to(dt)
+
+    def ones(n):
+        return torch.ones(n, device="cuda", dtype=dt)
+
+    layers, nbytes = [], 0
+    for kind in layer_types:
+        lw = dict(is_linear=kind, attn_norm=ones(hid), ffn_norm=ones(hid), w_gate=w(hid, inter), w_up=w(hid, inter),
+                  w_down=w(inter, hid))
+        if kind == 1:
+            lw.update(linear_in_qkv=w(hid, conv), linear_in_z=w(hid, vd), linear_in_b=w(hid, Hv),
+                      linear_in_a=w(hid, Hv), linear_conv1d_w=w(conv, 4, std=0.5), linear_dt_bias=w(Hv, std=0.1),
+                      linear_a_log=torch.log(torch.rand(Hv, generator=g, device="cuda") * 15 + 1).to(dt),
+                      linear_norm_w=ones(128), linear_out_proj=w(vd, hid))
+        else:
+            lw.update(wq=w(hid, 2 * qd), wk=w(hid, kvd), wv=w(hid, kvd), q_norm=ones(c["head_dim"]),
+                      k_norm=ones(c["head_dim"]), wo=w(qd, hid))
+        nbytes += sum(t.numel() * 2 for k, t in lw.items() if k != "is_linear")
+        layers.append(lw)
+    emb, fnorm, head = w(V, hid, std=1.0), ones(hid), w(hid, V)
+    weight_bytes = nbytes + (emb[0].numel() + fnorm.numel() + head.numel()) * 2  # one embedding row is read
+    model = q.ops.Model.from_weights(dict(c, layer_types=None), QIC_DTYPE_BF16, emb, fnorm, head, layers)
+    n_full = sum(1 for k in layer_types if k == 0)
+    kv_bytes = n_full * 2 * (context + 1) * kvd * 2
+    state_bytes = (len(layer_types) - n_full) * GdnConfig(num_k_heads=16, num_v_heads=32).state_bytes()
+    # the caches up to `context` hold whatever the first steps wrote; the timed step
+    # appends at `context` and attends over context + 1 tokens
+    model.set_position(1, context)
+    torch.cuda.synchronize()
+    logits = torch.empty(V, dtype=dt).pin_memory()
+
+    def e2e():
+        return model.decode(1, context, logits)
+
+    return dict(model=model, bytes=weight_bytes + kv_bytes + state_bytes, weight_bytes=weight_bytes,
+                kv_bytes=kv_bytes, state_bytes=state_bytes, e2e=e2e, keep=(layers, emb, fnorm, head),
+                config={"model": "Qwen3.5-4B-shaped hybrid, random bf16 weights", "layers": len(layer_types),
+                        "full_attention_layers": n_full, "context": context, "hidden": hid, "intermediate": inter,
+                        "vocab": V, "heads": f"{c['num_heads']}/{c['num_kv_heads']} x {c['head_dim']}",
+                        "launches_per_step": 2 + 5 * len(layer_types) + 1})
+
+
+def measure_decode_step(wl, steps, warmup, peaks):
+    """Device time of the captured step (CUDA events around `steps` replays) and the
+    end-to-end qic_model_decode (token copy, replay, greedy token and logits back,
+    synchronised), per token."""
+    m = wl["model"]
+    for _ in range(warmup):
+        m.step_graph()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        m.step_graph()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    for _ in range(warmup):
+        wl["e2e"]()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        wl["e2e"]()
+    ms_e2e = (time.perf_counter() - t0) * 1000 / steps
+    gbs = wl["bytes"] / (ms * 1e-3) / 1e9
+    return {"tokens_per_s": round(1000.0 / ms, 1), "ms_per_token": round(ms, 4), "value": round(gbs, 1),
+            "unit": "GB/s", "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes_per_token": int(wl["bytes"]),
+            "weight_bytes": int(wl["weight_bytes"]), "kv_bytes": int(wl["kv_bytes"]),
+            "state_bytes": int(wl["state_bytes"]),
+            "e2e": {"tokens_per_s": round(1000.0 / ms_e2e, 1), "ms_per_token": round(ms_e2e, 4),
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8 + 2 * wl["config"]["vocab"],
+                    "what": "qic_model_decode: token and position copied in, the step's graph, greedy token and "
+                            "logits copied out, synchronised (host wall clock)"},
+            "config": wl["config"]}
+
+
 def time_eager(fn, steps, warmup, world):
     """ms per call of fn (no graph): used for the NCCL all-gather path."""
     for _ in range(warmup):
@@ -1072,6 +1173,12 @@ def main():
             gl = capture(w2["library_step"])
             ml = time_graph(gl, args.steps, args.warmup, 1)
             del gl
+            # a whole decode step of a hybrid model through the decode-step runner
+            w3 = decode_step_workload()
+            extra["decode_step_qwen35_4b"] = measure_decode_step(w3, max(10, args.steps // 4), args.warmup, peaks)
+            w3["model"].close()
+            del w3
+            torch.cuda.empty_cache()
             extra["gemv_qwen3_8b"]["torch_cublas_unfused"] = {
                 "value": round(w2["bytes"] / (ml * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "us_per_model_layer": round(ml * 1000 / w2["config"]["layers"], 2),
