@@ -10,6 +10,9 @@
 //   gates:  beta = sigmoid(b), g = exp(-exp(A_log) * softplus(a + dt_bias))
 //   state:  S *= g; kv_mem = S^T k; S += k (beta (v - kv_mem))^T; o = S^T q
 //   out:    o * rsqrt(mean(o^2) + eps) * norm_w * silu(z)
+// The read-out uses o = (g S)^T q + (k . q) delta, equal to S'^T q, so the two column
+// sums over the state come from one pass and one reduction (with the q/k norms),
+// before the state update.
 //
 // Work split: one thread-block cluster per key head, holding the value heads that
 // share it (REP = Hv/Hk) times CB column blocks of the 128x128 fp32 state. Every CTA
@@ -58,9 +61,11 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   __shared__ float q_s[kGdnDk];
   __shared__ float k_s[kGdnDk];
   __shared__ float v_s[NC];
-  __shared__ float red[kGdnThreads / 32][NC];
+  __shared__ float red[kGdnThreads / 32][NC];   // warp partials of S_g^T q
+  __shared__ float redk[kGdnThreads / 32][NC];  // warp partials of S_g^T k
+  __shared__ float redn[kGdnThreads / 32][4];   // warp partials of |q|^2, |k|^2, k . q
+  __shared__ __align__(16) float delta_s[NC];
   __shared__ float col_s[NC];
-  __shared__ float scal[4];
   __shared__ float ssq_all[CB];  // the value head's CB partial sums of squares, pushed by their CTAs
 
   const T* qkv = static_cast<const T*>(a.qkv);
@@ -139,105 +144,113 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   __syncthreads();
 
-  // ---- 3. L2 norms of q and k, q scale (src/model.cpp:721-735) ----
-  {
-    const int w = tid >> 5, lane = tid & 31;
-    float sq = 0.0f, sk = 0.0f;
-    if (w == 0) {
-#pragma unroll
-      for (int i = lane; i < kGdnDk; i += 32) sq = __fadd_rn(sq, __fmul_rn(q_s[i], q_s[i]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-      if (lane == 0) scal[0] = 1.0f / sqrtf(sq + 1e-6f);
-    } else if (w == 1) {
-#pragma unroll
-      for (int i = lane; i < kGdnDk; i += 32) sk = __fadd_rn(sk, __fmul_rn(k_s[i], k_s[i]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sk += __shfl_xor_sync(0xffffffffu, sk, o);
-      if (lane == 0) scal[1] = 1.0f / sqrtf(sk + 1e-6f);
-    }
-  }
-  __syncthreads();
-  {
-    const float qscale = 1.0f / sqrtf(static_cast<float>(kGdnDk));
-    q_s[tid] = __fmul_rn(__fmul_rn(q_s[tid], scal[0]), qscale);
-    k_s[tid] = __fmul_rn(k_s[tid], scal[1]);
-  }
-  __syncthreads();
-
-  // ---- 4. gates (src/model.cpp:739-742) ----
+  // ---- 3-4. gates (src/model.cpp:739-742) ----
   const float bval = to_f32<T>(bv_raw);
   const float beta = 1.0f / (1.0f + expf(-bval));
   const float av = to_f32<T>(av_raw) + to_f32<T>(dt_raw);
   const float softp = log1pf(expf(av));
   const float g = expf(-expf(to_f32<T>(al_raw)) * softp);
 
-  // ---- 5. state block (loaded at the start): rows i = rg + RG*r, columns cb*NC + 4*quad .. +3 ----
-
-  auto block_colsum = [&](float4 part) {
-    // sum `part` over all threads with the same quad, result in col_s[4*quad + 0..3]
-#pragma unroll
-    for (int o = QUADS; o < 32; o <<= 1) {
-      part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
-      part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
-      part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
-      part.w += __shfl_xor_sync(0xffffffffu, part.w, o);
-    }
-    const int w = tid >> 5, lane = tid & 31;
-    if (lane < QUADS) {
-      red[w][4 * quad + 0] = part.x;
-      red[w][4 * quad + 1] = part.y;
-      red[w][4 * quad + 2] = part.z;
-      red[w][4 * quad + 3] = part.w;
-    }
-    __syncthreads();
-    if (tid < NC) {
-      float acc = 0.0f;
-#pragma unroll
-      for (int ww = 0; ww < kGdnThreads / 32; ++ww) acc += red[ww][tid];
-      col_s[tid] = acc;
-    }
-    __syncthreads();
-  };
-
-  // decay, then kv_mem = S^T k
-  float4 part = make_float4(0.f, 0.f, 0.f, 0.f);
+  // ---- 5. one pass over the decayed state (src/model.cpp:721-775) ----
+  // With q^ = q / |q| / sqrt(dk), k^ = k / |k| and S_g = g S (the decayed state):
+  //   kv_mem = S_g^T k^,  delta = beta (v - kv_mem),  S' = S_g + k^ delta^T,
+  //   o = S'^T q^ = S_g^T q^ + (k^ . q^) delta.
+  // So the column sums S_g^T q and S_g^T k (raw conv outputs, scaled afterwards) and
+  // the sums |q|^2, |k|^2 and k . q come out of one reduction, and the state update
+  // is off the output's path. The state rows of this CTA were loaded at the start:
+  // rows i = rg + RG*r, columns cb*NC + 4*quad .. +3.
+  float4 pq = make_float4(0.f, 0.f, 0.f, 0.f), pk = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int r = 0; r < RPT; ++r) {
+    const float qr = q_s[rg + RG * r];
     const float kr = k_s[rg + RG * r];
     s[r].x = __fmul_rn(s[r].x, g);
     s[r].y = __fmul_rn(s[r].y, g);
     s[r].z = __fmul_rn(s[r].z, g);
     s[r].w = __fmul_rn(s[r].w, g);
-    part.x = __fadd_rn(part.x, __fmul_rn(s[r].x, kr));
-    part.y = __fadd_rn(part.y, __fmul_rn(s[r].y, kr));
-    part.z = __fadd_rn(part.z, __fmul_rn(s[r].z, kr));
-    part.w = __fadd_rn(part.w, __fmul_rn(s[r].w, kr));
+    pq.x = __fadd_rn(pq.x, __fmul_rn(s[r].x, qr));
+    pq.y = __fadd_rn(pq.y, __fmul_rn(s[r].y, qr));
+    pq.z = __fadd_rn(pq.z, __fmul_rn(s[r].z, qr));
+    pq.w = __fadd_rn(pq.w, __fmul_rn(s[r].w, qr));
+    pk.x = __fadd_rn(pk.x, __fmul_rn(s[r].x, kr));
+    pk.y = __fadd_rn(pk.y, __fmul_rn(s[r].y, kr));
+    pk.z = __fadd_rn(pk.z, __fmul_rn(s[r].z, kr));
+    pk.w = __fadd_rn(pk.w, __fmul_rn(s[r].w, kr));
   }
-  block_colsum(part);
-  // delta = beta (v - kv_mem); S += k delta^T; o = S^T q
-  float4 delta;
-  delta.x = __fmul_rn(v_s[4 * quad + 0] - col_s[4 * quad + 0], beta);
-  delta.y = __fmul_rn(v_s[4 * quad + 1] - col_s[4 * quad + 1], beta);
-  delta.z = __fmul_rn(v_s[4 * quad + 2] - col_s[4 * quad + 2], beta);
-  delta.w = __fmul_rn(v_s[4 * quad + 3] - col_s[4 * quad + 3], beta);
-  __syncthreads();  // col_s is reused below
-  part = make_float4(0.f, 0.f, 0.f, 0.f);
+  // channel tid's contributions to |q|^2, |k|^2 and k . q
+  float nq = __fmul_rn(q_s[tid], q_s[tid]), nk = __fmul_rn(k_s[tid], k_s[tid]), nqk = __fmul_rn(q_s[tid], k_s[tid]);
+  const int w = tid >> 5, lane = tid & 31;
 #pragma unroll
-  for (int r = 0; r < RPT; ++r) {
-    const float kr = k_s[rg + RG * r];
-    const float qr = q_s[rg + RG * r];
-    s[r].x = __fadd_rn(s[r].x, __fmul_rn(kr, delta.x));
-    s[r].y = __fadd_rn(s[r].y, __fmul_rn(kr, delta.y));
-    s[r].z = __fadd_rn(s[r].z, __fmul_rn(kr, delta.z));
-    s[r].w = __fadd_rn(s[r].w, __fmul_rn(kr, delta.w));
-    part.x = __fadd_rn(part.x, __fmul_rn(s[r].x, qr));
-    part.y = __fadd_rn(part.y, __fmul_rn(s[r].y, qr));
-    part.z = __fadd_rn(part.z, __fmul_rn(s[r].z, qr));
-    part.w = __fadd_rn(part.w, __fmul_rn(s[r].w, qr));
-    *reinterpret_cast<float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv) = s[r];
+  for (int o = QUADS; o < 32; o <<= 1) {
+    pq.x += __shfl_xor_sync(0xffffffffu, pq.x, o);
+    pq.y += __shfl_xor_sync(0xffffffffu, pq.y, o);
+    pq.z += __shfl_xor_sync(0xffffffffu, pq.z, o);
+    pq.w += __shfl_xor_sync(0xffffffffu, pq.w, o);
+    pk.x += __shfl_xor_sync(0xffffffffu, pk.x, o);
+    pk.y += __shfl_xor_sync(0xffffffffu, pk.y, o);
+    pk.z += __shfl_xor_sync(0xffffffffu, pk.z, o);
+    pk.w += __shfl_xor_sync(0xffffffffu, pk.w, o);
   }
-  block_colsum(part);  // col_s = o for this CTA's columns
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    nq += __shfl_xor_sync(0xffffffffu, nq, o);
+    nk += __shfl_xor_sync(0xffffffffu, nk, o);
+    nqk += __shfl_xor_sync(0xffffffffu, nqk, o);
+  }
+  if (lane < QUADS) {
+    red[w][4 * quad + 0] = pq.x;
+    red[w][4 * quad + 1] = pq.y;
+    red[w][4 * quad + 2] = pq.z;
+    red[w][4 * quad + 3] = pq.w;
+    redk[w][4 * quad + 0] = pk.x;
+    redk[w][4 * quad + 1] = pk.y;
+    redk[w][4 * quad + 2] = pk.z;
+    redk[w][4 * quad + 3] = pk.w;
+  }
+  if (lane == 0) {
+    redn[w][0] = nq;
+    redn[w][1] = nk;
+    redn[w][2] = nqk;
+  }
+  __syncthreads();
+  // the norms (every thread, warps summed in order)
+  float sq = 0.0f, sk = 0.0f, sqk = 0.0f;
+#pragma unroll
+  for (int ww = 0; ww < kGdnThreads / 32; ++ww) {
+    sq += redn[ww][0];
+    sk += redn[ww][1];
+    sqk += redn[ww][2];
+  }
+  const float inv_q = 1.0f / sqrtf(sq + 1e-6f);
+  const float inv_k = 1.0f / sqrtf(sk + 1e-6f);
+  const float qscale = __fmul_rn(inv_q, 1.0f / sqrtf(static_cast<float>(kGdnDk)));
+  const float kq = __fmul_rn(__fmul_rn(sqk, inv_k), qscale);  // k^ . q^
+  if (tid < NC) {
+    float cq_sum = 0.0f, ck_sum = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < kGdnThreads / 32; ++ww) {
+      cq_sum += red[ww][tid];
+      ck_sum += redk[ww][tid];
+    }
+    const float kv_mem = __fmul_rn(ck_sum, inv_k);
+    const float delta = __fmul_rn(v_s[tid] - kv_mem, beta);
+    delta_s[tid] = delta;
+    col_s[tid] = __fadd_rn(__fmul_rn(cq_sum, qscale), __fmul_rn(kq, delta));  // o
+  }
+  __syncthreads();
+  // the new state: S' = S_g + k^ delta^T
+  {
+    const float4 delta = *reinterpret_cast<const float4*>(&delta_s[4 * quad]);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+      const float kr = __fmul_rn(k_s[rg + RG * r], inv_k);
+      s[r].x = __fadd_rn(s[r].x, __fmul_rn(kr, delta.x));
+      s[r].y = __fadd_rn(s[r].y, __fmul_rn(kr, delta.y));
+      s[r].z = __fadd_rn(s[r].z, __fmul_rn(kr, delta.z));
+      s[r].w = __fadd_rn(s[r].w, __fmul_rn(kr, delta.w));
+      *reinterpret_cast<float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv) = s[r];
+    }
+  }
 
   // ---- 6. gated RMSNorm over the value head's 128 columns (src/model.cpp:777-791) ----
   float ss_mine = 0.0f;  // this CTA's sum of squares (warp 0)
