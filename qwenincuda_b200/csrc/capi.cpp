@@ -90,8 +90,8 @@ size_t bytes_to_allocation_end(const void* p) {
 // every 64-element chunk of one head for box_h token rows. Shared memory receives the
 // box chunk-major ([chunk][token][128 B], 128-byte swizzle), the layout the consumer
 // warps index.
-int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens, int kv_dim, int head_dim,
-                  int box_h) {
+int encode_kv_map_uncached(CUtensorMap* map, int dtype, const void* base, int64_t tokens, int kv_dim, int head_dim,
+                           int box_h) {
   load_driver_entry_points();
   if (g_encode == nullptr) return QIC_ERROR_CUDA;
   cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(kv_dim / 64)};
@@ -105,10 +105,56 @@ int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens,
   return r == CUDA_SUCCESS ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
 }
 
+// Encoded maps of recent calls, per host thread: a decode loop encodes the same
+// (cache, shape) maps at every step. The key holds every argument of the encoding, so
+// a hit is the map that encoding would produce (also after the memory at `base` was
+// freed and allocated again).
+struct MapKey {
+  int kind;  // 0: K/V cache map, 1: GEMV weight map
+  const void* base;
+  int64_t tokens;
+  int dtype, kv_dim, head_dim, box_h;
+  bool operator==(const MapKey& o) const {
+    return kind == o.kind && base == o.base && tokens == o.tokens && dtype == o.dtype && kv_dim == o.kv_dim &&
+           head_dim == o.head_dim && box_h == o.box_h;
+  }
+};
+
+template <typename Encode>
+int encode_cached(CUtensorMap* map, const MapKey& key, Encode encode) {
+  constexpr int kEntries = 256;  // e.g. K and V of 64 layers plus their projections
+  struct Entry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+  };
+  thread_local std::vector<Entry> cache(kEntries);
+  const size_t h = (reinterpret_cast<uintptr_t>(key.base) >> 8) ^ static_cast<size_t>(key.tokens) * 31u ^
+                   static_cast<size_t>(key.box_h * 7 + key.head_dim + key.dtype + key.kind * 131 + key.kv_dim);
+  Entry& e = cache[h % kEntries];
+  if (e.used && e.key == key) {
+    *map = e.map;
+    return QIC_SUCCESS;
+  }
+  const int rc = encode(map);
+  if (rc == QIC_SUCCESS) {
+    e.key = key;
+    e.map = *map;
+    e.used = true;
+  }
+  return rc;
+}
+
+int encode_kv_map(CUtensorMap* map, int dtype, const void* base, int64_t tokens, int kv_dim, int head_dim, int box_h) {
+  return encode_cached(map, MapKey{0, base, tokens, dtype, kv_dim, head_dim, box_h}, [&](CUtensorMap* m) {
+    return encode_kv_map_uncached(m, dtype, base, tokens, kv_dim, head_dim, box_h);
+  });
+}
+
 // GEMV weights [K rows, N columns] (N contiguous) as a 2D tensor {N, K}; one box is
 // kGemvTile columns of kGemvRowsPerSlot rows, row-major in shared memory, zeros past
 // either edge.
-int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int K, int N) {
+int encode_weight_map_uncached(CUtensorMap* map, int dtype, const void* w, int K, int N) {
   load_driver_entry_points();
   if (g_encode == nullptr) return QIC_ERROR_CUDA;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K)};
@@ -120,6 +166,11 @@ int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int K, int N) 
                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QIC_SUCCESS : QIC_ERROR_INVALID_VALUE;
+}
+
+int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int K, int N) {
+  return encode_cached(map, MapKey{1, w, K, dtype, N, 0, 0},
+                       [&](CUtensorMap* m) { return encode_weight_map_uncached(m, dtype, w, K, N); });
 }
 
 bool valid_dtype(int d) { return d == QIC_DTYPE_F16 || d == QIC_DTYPE_BF16; }

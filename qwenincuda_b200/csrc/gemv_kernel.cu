@@ -314,11 +314,27 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
 namespace {
 
+// Kernel attributes, set once per device: the largest dynamic shared memory any launch
+// uses, and clusters above 8 CTAs.
+template <typename T, bool PAIR, bool NORM>
+cudaError_t configure_gemv() {
+  static unsigned long long configured = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && (configured & (1ull << dev))) return cudaSuccess;
+  auto kern = gemv_kernel<T, PAIR, NORM>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(gemv_smem_bytes(kGemvMaxRowsPerSplit)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && dev < 64) configured |= 1ull << dev;
+  return e;
+}
+
 template <typename T, bool PAIR, bool NORM>
 cudaError_t launch_gemv_typed(const GemvParams& p, size_t smem, cudaStream_t stream) {
   auto kern = gemv_kernel<T, PAIR, NORM>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = configure_gemv<T, PAIR, NORM>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.n_tiles, 1);
@@ -348,8 +364,7 @@ cudaError_t launch_gemv_dtype(const GemvParams& p, size_t smem, bool pair, bool 
 template <typename T>
 int max_clusters_typed(int cluster, size_t smem) {
   auto kern = gemv_kernel<T, false, true>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess ||
-      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+  if (configure_gemv<T, false, true>() != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
