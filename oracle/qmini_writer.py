@@ -52,8 +52,12 @@ class QminiConfig:
         return len(self.layer_types)
 
 
-def write_qmini(path, cfg: QminiConfig, seed: int = 0) -> None:
+def write_qmini(path, cfg: QminiConfig, seed: int = 0) -> dict:
+    """Writes the file and returns its tensors as fp16 numpy arrays: tok_embeddings,
+    final_norm, lm_head and `layers` (one dict per layer, keyed like the reference's
+    LayerWeights members)."""
     rng = np.random.default_rng(seed)
+    out = {"layers": []}
     H, Hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
     hid, inter, vocab = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
     q_dim, kv_dim = H * d, Hkv * d
@@ -63,10 +67,13 @@ def write_qmini(path, cfg: QminiConfig, seed: int = 0) -> None:
     Hv = cfg.linear_num_value_heads
 
     with open(path, "wb") as f:
-        def tensor(a):
-            a = np.ascontiguousarray(a, dtype=np.float16).ravel()
-            f.write(struct.pack("<Q", a.size))
-            f.write(a.tobytes())
+        def tensor(a, name=None, layer=None):
+            a = np.ascontiguousarray(a, dtype=np.float16)
+            flat = a.ravel()
+            f.write(struct.pack("<Q", flat.size))
+            f.write(flat.tobytes())
+            if name is not None:
+                (out if layer is None else layer)[name] = a
 
         def proj(n_in, n_out):
             return rng.standard_normal((n_in, n_out), dtype=np.float32) / np.sqrt(n_in)
@@ -81,29 +88,33 @@ def write_qmini(path, cfg: QminiConfig, seed: int = 0) -> None:
                             cfg.linear_conv_kernel_dim, cfg.max_seq_len))
         f.write(struct.pack("<2f", cfg.rms_norm_eps, cfg.rope_theta))
         f.write(struct.pack(f"<{cfg.num_layers}i", *cfg.layer_types))
-        tensor(rng.standard_normal((vocab, hid), dtype=np.float32))
+        tensor(rng.standard_normal((vocab, hid), dtype=np.float32), "tok_embeddings")
         for kind in cfg.layer_types:
-            tensor(norm(hid))
+            lw = {"is_linear": kind}
+            out["layers"].append(lw)
+            tensor(norm(hid), "attn_norm", lw)
             if kind == 1:
-                tensor(proj(hid, conv_dim))
-                tensor(proj(hid, val_dim))
-                tensor(proj(hid, Hv))
-                tensor(proj(hid, Hv))
-                tensor(0.5 * rng.standard_normal((conv_dim, cfg.linear_conv_kernel_dim), dtype=np.float32))
-                tensor(0.1 * rng.standard_normal(Hv, dtype=np.float32))
-                tensor(np.log(rng.uniform(1.0, 16.0, Hv)).astype(np.float32))
-                tensor(norm(cfg.linear_value_head_dim))
-                tensor(proj(val_dim, hid))
+                tensor(proj(hid, conv_dim), "linear_in_qkv", lw)
+                tensor(proj(hid, val_dim), "linear_in_z", lw)
+                tensor(proj(hid, Hv), "linear_in_b", lw)
+                tensor(proj(hid, Hv), "linear_in_a", lw)
+                tensor(0.5 * rng.standard_normal((conv_dim, cfg.linear_conv_kernel_dim), dtype=np.float32),
+                       "linear_conv1d_w", lw)
+                tensor(0.1 * rng.standard_normal(Hv, dtype=np.float32), "linear_dt_bias", lw)
+                tensor(np.log(rng.uniform(1.0, 16.0, Hv)).astype(np.float32), "linear_a_log", lw)
+                tensor(norm(cfg.linear_value_head_dim), "linear_norm_w", lw)
+                tensor(proj(val_dim, hid), "linear_out_proj", lw)
             else:
-                tensor(proj(hid, 2 * q_dim))
-                tensor(proj(hid, kv_dim))
-                tensor(proj(hid, kv_dim))
-                tensor(norm(d))
-                tensor(norm(d))
-                tensor(proj(q_dim, hid))
-            tensor(norm(hid))
-            tensor(proj(hid, inter))
-            tensor(proj(hid, inter))
-            tensor(proj(inter, hid))
-        tensor(norm(hid))
-        tensor(proj(hid, vocab))
+                tensor(proj(hid, 2 * q_dim), "wq", lw)
+                tensor(proj(hid, kv_dim), "wk", lw)
+                tensor(proj(hid, kv_dim), "wv", lw)
+                tensor(norm(d), "q_norm", lw)
+                tensor(norm(d), "k_norm", lw)
+                tensor(proj(q_dim, hid), "wo", lw)
+            tensor(norm(hid), "ffn_norm", lw)
+            tensor(proj(hid, inter), "w_gate", lw)
+            tensor(proj(hid, inter), "w_up", lw)
+            tensor(proj(inter, hid), "w_down", lw)
+        tensor(norm(hid), "final_norm")
+        tensor(proj(hid, vocab), "lm_head")
+    return out

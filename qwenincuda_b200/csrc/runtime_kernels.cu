@@ -25,19 +25,40 @@ __global__ void __launch_bounds__(256) embed_kernel(const T* __restrict__ table,
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// One CTA: the first index of the largest value (NaN never wins: comparisons are false).
+// One CTA: the first index of the largest value, starting from -1e30 like
+// argmax_host (NaN never wins: comparisons are false). n is a multiple of 8: every
+// thread reads 16-byte vectors, four in flight, in increasing index order.
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, int n, int32_t* __restrict__ out) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float sv[32];
   __shared__ int si[32];
-  float best = -INFINITY;
+  constexpr int U = 4;
+  const int nv = n / 8;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  float best = -1e30f;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = to_f32<T>(x[i]);
-    if (v > best) {  // ascending i: the first of equal values stays
-      best = v;
-      bi = i;
+  for (int base = threadIdx.x; base < nv; base += blockDim.x * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      v[u] = i < nv ? xv[i] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < nv) {
+        const T* e = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float f = to_f32<T>(e[k]);
+          if (f > best) {  // ascending index within the thread: the first of equal values stays
+            best = f;
+            bi = i * 8 + k;
+          }
+        }
+      }
     }
   }
   auto better = [](float v, int i, float w, int j) { return w > v || (w == v && j < i); };
@@ -58,7 +79,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, i
   __syncthreads();
   if (warp == 0) {
     const int nw = blockDim.x >> 5;
-    best = lane < nw ? sv[lane] : -INFINITY;
+    best = lane < nw ? sv[lane] : -1e30f;
     bi = lane < nw ? si[lane] : 0x7fffffff;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -39,8 +39,8 @@ STEPS = 24
 def synth(tmp_path_factory):
     path = tmp_path_factory.mktemp("qmini") / "synth_qwen35.qmini"
     cfg = QminiConfig()
-    write_qmini(path, cfg, seed=11)
-    return path, cfg
+    tensors = write_qmini(path, cfg, seed=11)
+    return path, cfg, tensors
 
 
 def _prompt(cfg, n, seed=5):
@@ -54,7 +54,7 @@ def _close(a, b):
 
 
 def test_runner_matches_reference_decode_next(synth):
-    path, cfg = synth
+    path, cfg, _ = synth
     ref = RefQwenModel(path)
     ours = q.ops.Model.load(path)
     try:
@@ -89,6 +89,33 @@ def test_runner_matches_reference_decode_next(synth):
         ref.close()
 
 
+def test_runner_over_device_weights_matches_file_runner(synth):
+    """qic_model_create over the same weights as device tensors (the caller's buffers,
+    LayerWeights layout) gives the bits of qic_model_load's runner, step after step."""
+    path, cfg, t = synth
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    layers = [{k: (v if k == "is_linear" else dev(v)) for k, v in lw.items()} for lw in t["layers"]]
+    conf = dict(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
+                num_layers=cfg.num_layers, num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads,
+                head_dim=cfg.head_dim, linear_num_key_heads=cfg.linear_num_key_heads,
+                linear_num_value_heads=cfg.linear_num_value_heads, linear_key_head_dim=cfg.linear_key_head_dim,
+                linear_value_head_dim=cfg.linear_value_head_dim, linear_conv_kernel_dim=cfg.linear_conv_kernel_dim,
+                max_seq_len=cfg.max_seq_len, rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta)
+    created = q.ops.Model.from_weights(conf, q.QIC_DTYPE_F16, dev(t["tok_embeddings"]), dev(t["final_norm"]),
+                                       dev(t["lm_head"]), layers)
+    loaded = q.ops.Model.load(path)
+    try:
+        a = torch.empty(cfg.vocab_size, dtype=torch.float16)
+        b = torch.empty(cfg.vocab_size, dtype=torch.float16)
+        for pos, tok in enumerate(_prompt(cfg, 40, seed=7)):
+            na = created.decode(tok, pos, a)
+            nb = loaded.decode(tok, pos, b)
+            assert na == nb and torch.equal(a.view(torch.int16), b.view(torch.int16)), f"position {pos}"
+    finally:
+        created.close()
+        loaded.close()
+
+
 def _run(exe, path, ids, steps):
     out = subprocess.run([str(exe), "--model", str(path), "--input-ids", ",".join(map(str, ids)),
                           "--max-new-tokens", str(steps), "--greedy-after", "0", "--dump-topk", "5",
@@ -104,7 +131,7 @@ def _run(exe, path, ids, steps):
 
 
 def test_dropin_executable_matches_reference_executable(synth):
-    path, cfg = synth
+    path, cfg, _ = synth
     exe_ref, exe_qic = REF_DIR / "qwen_minimal_ref", REF_DIR / "qwen_minimal_qic"
     if not exe_ref.exists() or not exe_qic.exists():
         pytest.fail("oracle/_ref executables not built (make -C oracle ref REF=<reference project root>)")
