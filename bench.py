@@ -669,6 +669,51 @@ def measure_decode_step(wl, steps, warmup, peaks):
             "config": wl["config"]}
 
 
+def decode_step_vs_reference(steps=20, warmup=3, context=512):
+    """The reference's own decode loop against this library's runner on the same
+    synthetic qmini v4 file (Qwen3.5-4B widths, 8 layers: 6 GatedDeltaNet and 2 gated
+    full attention; vocab 32768; fp16, the format's type): QwenMiniModel::decode_next
+    (src/model.cpp:823-845, built unmodified into oracle/_ref) and qic_model_decode,
+    each timed end to end per token (host wall clock, synchronised) at position
+    `context` after a prefill of `context` tokens."""
+    import tempfile
+
+    import qwenincuda_b200 as q
+    from oracle.oracle import RefQwenModel
+    from oracle.qmini_writer import QminiConfig, write_qmini
+
+    cfg = QminiConfig(vocab_size=32768, hidden_size=2560, intermediate_size=9216, num_heads=16, num_kv_heads=4,
+                      head_dim=256, linear_num_key_heads=16, linear_num_value_heads=32, max_seq_len=context + steps
+                      + warmup + 8, layer_types=[1, 1, 1, 0, 1, 1, 1, 0])
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "synth_qwen35_8l.qmini"
+        write_qmini(path, cfg, seed=3)
+        res = {}
+        for name, make in (("reference_decode_next", lambda: RefQwenModel(path)),
+                           ("qic_model_decode", lambda: q.ops.Model.load(path))):
+            m = make()
+            try:
+                for pos in range(context):  # prefill, token by token as the reference's generate does
+                    m.decode(pos % cfg.vocab_size, pos)
+                pos = context
+                for _ in range(warmup):
+                    m.decode(1, pos)
+                    pos += 1
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                for _ in range(steps):
+                    m.decode(1, pos)
+                    pos += 1
+                ms = (time.perf_counter() - t0) * 1000 / steps
+            finally:
+                m.close()
+            res[name] = {"ms_per_token": round(ms, 3), "tokens_per_s": round(1000 / ms, 1)}
+    res["speedup"] = round(res["reference_decode_next"]["ms_per_token"] / res["qic_model_decode"]["ms_per_token"], 1)
+    res["what"] = ("same synthetic qmini v4 file (Qwen3.5-4B widths, 8 layers, vocab 32768, fp16), position "
+                   f"{context}; end to end per token, host wall clock")
+    return res
+
+
 def time_eager(fn, steps, warmup, world):
     """ms per call of fn (no graph): used for the NCCL all-gather path."""
     for _ in range(warmup):
@@ -1179,6 +1224,10 @@ def main():
             w3["model"].close()
             del w3
             torch.cuda.empty_cache()
+            try:  # the reference's own decode loop on the same file (its build lives in oracle/_ref)
+                extra["decode_step_qwen35_4b"]["vs_reference_decode_next"] = decode_step_vs_reference()
+            except Exception as exc:  # extra information only
+                extra["decode_step_qwen35_4b"]["vs_reference_decode_next"] = {"unavailable": str(exc)[:200]}
             extra["gemv_qwen3_8b"]["torch_cublas_unfused"] = {
                 "value": round(w2["bytes"] / (ml * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "us_per_model_layer": round(ml * 1000 / w2["config"]["layers"], 2),
