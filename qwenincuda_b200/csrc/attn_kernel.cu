@@ -47,7 +47,10 @@
 //    drains its own copies (bounded) and exits.
 //
 // Compiled with --use_fast_math so the fused norm / RoPE / gate arithmetic matches
-// the reference build bit for bit.
+// the reference build bit for bit where bytes are stored and compared: the appended k
+// row (head norm with the reference's ascending sum order, RoPE) and the gate. The q
+// rows' head norm sums its squares with a shuffle tree: q feeds only the attention
+// output, which is checked within tolerance.
 #include "qic_internal.h"
 #include "rowops.cuh"
 
@@ -68,7 +71,8 @@ struct AttnShape {
   static constexpr int kCtrlBytes = 128;                         // full[] barriers
   static constexpr int kQBytes = kMaxGroup * D * 2;
   static constexpr int kFlagBytes = 64;
-  static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes;
+  static constexpr int kMlBytes = 2 * kConsumerWarps * 8 * 4;       // every warp's (m, l) per head column
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes + kMlBytes;
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -138,6 +142,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + Sh::kRingBytes);
   T* q_s = reinterpret_cast<T*>(ring + Sh::kRingBytes + Sh::kCtrlBytes);
   volatile int* flags_s = reinterpret_cast<volatile int*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes);
+  // [4][8] m then [4][8] l of the warps, written as each warp leaves its stage loop
+  float* ml_s = reinterpret_cast<float*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes);
   // flags_s[0]: abort, flags_s[1]: this CTA merges
 
   const int warp = threadIdx.x >> 5;
@@ -339,14 +345,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     if (r0 < G) {
       if (fuse_q) {
-        row_rmsnorm_w<T, D>(v0, qw, hd, p.eps);
+        row_rmsnorm_w_tree<T, D>(v0, qw, hd, p.eps);
         row_rope<T, D>(v0, hd, rpos, p.theta, lane);
       }
       row_store<T, D>(q_s + r0 * D, v0, lane);
     }
     if (r1 < G) {
       if (fuse_q) {
-        row_rmsnorm_w<T, D>(v1, qw, hd, p.eps);
+        row_rmsnorm_w_tree<T, D>(v1, qw, hd, p.eps);
         row_rope<T, D>(v1, hd, rpos, p.theta, lane);
       }
       row_store<T, D>(q_s + r1 * D, v1, lane);
@@ -580,6 +586,17 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     l0 += __shfl_xor_sync(kFullMask, l0, o);
     l1 += __shfl_xor_sync(kFullMask, l1, o);
   }
+  const int hA = (lane & 3) * 2, hB = hA + 1;
+  // this warp's (m, l) go outside the ring (other warps may still read their slots),
+  // so one barrier both ends the stage loops and publishes them
+  float* cm = ml_s;                    // [4][8] m
+  float* cl = ml_s + kConsumerWarps * 8;  // [4][8] l
+  if (lane < 4) {
+    cm[warp * 8 + hA] = m0;
+    cm[warp * 8 + hB] = m1;
+    cl[warp * 8 + hA] = l0;
+    cl[warp * 8 + hB] = l1;
+  }
   consumer_sync();
   const bool aborted = flags_s[0] != 0;
 
@@ -587,21 +604,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   // Each warp's share of head h is weighted by exp2(m_w - M) / L with M, L the
   // head's maximum and normaliser over the four warps; the weights are applied to
   // the accumulators in registers, so the cross-warp step is a plain sum.
-  float* cm = reinterpret_cast<float*>(ring);  // [4][8] m
-  float* cl = cm + kConsumerWarps * 8;         // [4][8] l
-  float* co = cl + kConsumerWarps * 8;         // [4][8][D + 4] weighted o (padded rows: no bank conflicts)
+  float* co = reinterpret_cast<float*>(ring);  // [4][8][D + 4] weighted o (padded rows: no bank conflicts)
   float* mine = reinterpret_cast<float*>(ring + Sh::kCombineBytes);  // this split: [o: G*D][lse: G]
   constexpr int kCoRow = D + 4;
-  const int hA = (lane & 3) * 2, hB = hA + 1;
-  if (!aborted) {
-    if (lane < 4) {
-      cm[warp * 8 + hA] = m0;
-      cm[warp * 8 + hB] = m1;
-      cl[warp * 8 + hA] = l0;
-      cl[warp * 8 + hB] = l1;
-    }
-  }
-  consumer_sync();
   if (!aborted) {
     float MA = -INFINITY, MB = -INFINITY;
 #pragma unroll

@@ -98,6 +98,26 @@ __device__ __forceinline__ void row_rmsnorm_w(float (&v)[D / 32], const float (&
   }
 }
 
+// row_rmsnorm_w with the sum of squares reduced as a butterfly (5 shuffle steps instead
+// of the 32*E-step ordered chain): for rows whose bytes only feed tolerance-checked
+// results (q), not rows stored for byte comparison (the appended k).
+template <typename T, int D>
+__device__ __forceinline__ void row_rmsnorm_w_tree(float (&v)[D / 32], const float (&wv)[D / 32], int head_dim,
+                                                   float eps) {
+  constexpr int E = D / 32;
+  float ssum = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ssum = __fadd_rn(ssum, __fmul_rn(v[e], v[e]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(kFullMask, ssum, o);
+  float inv_rms = rsqrtf(ssum / static_cast<float>(head_dim) + eps);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    float xv = v[e];
+    v[e] = to_f32<T>(from_f32<T>(xv * inv_rms * wv[e]));
+  }
+}
+
 // In place: v = T(v * rsqrt(mean(v^2) + eps) * w).
 template <typename T, int D>
 __device__ __forceinline__ void row_rmsnorm(float (&v)[D / 32], const T* __restrict__ w, int head_dim, float eps,
