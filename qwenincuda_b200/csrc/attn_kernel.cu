@@ -330,6 +330,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
   }
   const bool app_ok = app_slot >= 0 && app_slot < p.cache_tokens;
+  // the rotation at rpos (the same for q and the appended k), before the wait
+  float rc[D / 32], rs[D / 32];
+  if (fuse_q || my_append) row_rope_coeffs<D>(rc, rs, hd, rpos, p.theta, lane);
   // inputs written by the preceding kernel are read only after it has completed
   pdl_wait();
   // ---- prologue: q rows into shared memory, and the fused append ----
@@ -346,21 +349,21 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (r0 < G) {
       if (fuse_q) {
         row_rmsnorm_w_tree<T, D>(v0, qw, hd, p.eps);
-        row_rope<T, D>(v0, hd, rpos, p.theta, lane);
+        row_rope_apply<T, D>(v0, rc, rs, lane);
       }
       row_store<T, D>(q_s + r0 * D, v0, lane);
     }
     if (r1 < G) {
       if (fuse_q) {
         row_rmsnorm_w_tree<T, D>(v1, qw, hd, p.eps);
-        row_rope<T, D>(v1, hd, rpos, p.theta, lane);
+        row_rope_apply<T, D>(v1, rc, rs, lane);
       }
       row_store<T, D>(q_s + r1 * D, v1, lane);
     }
     if (my_append) {
       if (app_ok) {
         row_rmsnorm_w<T, D>(kr, kw, hd, p.eps);
-        row_rope<T, D>(kr, hd, rpos, p.theta, lane);
+        row_rope_apply<T, D>(kr, rc, rs, lane);
         const size_t at = static_cast<size_t>(app_slot) * static_cast<size_t>(p.Hkv) * D + static_cast<size_t>(kvh) * D;
         row_store<T, D>(static_cast<T*>(p.k_cache) + at, kr, lane);
         row_store<T, D>(static_cast<T*>(p.v_cache) + at, vr, lane);

@@ -150,4 +150,37 @@ __device__ __forceinline__ void row_rope(float (&v)[D / 32], int head_dim, int p
   }
 }
 
+// row_rope in two halves: the rotation of this lane's elements at `position` (depends
+// on neither row, so it can be computed before the row is loaded), then its application.
+// The same expressions as row_rope, so the same bytes.
+template <int D>
+__device__ __forceinline__ void row_rope_coeffs(float (&c)[D / 32], float (&sn)[D / 32], int head_dim, int position,
+                                                float rope_theta, int lane) {
+  constexpr int E = D / 32;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    int d = (lane & 15) * E + e;
+    float inv_freq = powf(rope_theta, -2.0f * static_cast<float>(d) / static_cast<float>(head_dim));
+    float angle = static_cast<float>(position) * inv_freq;
+    c[e] = cosf(angle);
+    sn[e] = sinf(angle);
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void row_rope_apply(float (&v)[D / 32], const float (&c)[D / 32], const float (&sn)[D / 32],
+                                               int lane) {
+  constexpr int E = D / 32;
+  const bool first = lane < 16;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    float other = __shfl_xor_sync(kFullMask, v[e], 16);
+    float x0 = first ? v[e] : other;
+    float x1 = first ? other : v[e];
+    float y0 = x0 * c[e] - x1 * sn[e];
+    float y1 = x1 * c[e] + x0 * sn[e];
+    v[e] = to_f32<T>(from_f32<T>(first ? y0 : y1));
+  }
+}
+
 }  // namespace qic
