@@ -415,6 +415,9 @@ typedef struct qic_gdn_args {
   float* conv_state;        /* [conv_dim, K] fp32, updated in place */
   float* recurrent_state;   /* [Hv, dk, dv] fp32, updated in place */
   void* out;                /* [Hv*dv] gated-norm output (input of out_proj) */
+  int32_t* status;          /* optional device word (NULL: none): QIC_DEV_TIMEOUT is OR-ed in if a
+                               CTA gives up waiting for its value head's peers (the output of that
+                               head is then not written) */
 } qic_gdn_args;
 
 /* One decode step of src/model.cpp:692-791 on the device: conv-state shift and causal

@@ -159,6 +159,7 @@ class GdnArgs(ctypes.Structure):
         ("conv_state", ctypes.c_void_p),
         ("recurrent_state", ctypes.c_void_p),
         ("out", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
     ]
 
 

@@ -28,13 +28,14 @@
 //    the interleaved q/gate projection), the K/V append of the new token (head
 //    RMSNorm + RoPE of k written into its page slot before the stage holding it is
 //    copied), and the sigmoid output gate.
-//  * The splits of a kv head form thread-block clusters. Each CTA leaves its (o, lse)
-//    partial in shared memory; after a cluster barrier every CTA merges one slice of
-//    the outputs from all partials of its cluster through distributed shared memory,
-//    then arrives (relaxed) at the second barrier phase, whose wait is the kernel's
-//    last instruction. When a kv head spans several clusters, each cluster slice is
-//    written to the caller's workspace and the last arriving CTA of that slice
-//    (release/acquire counter) merges the cluster partials by log-sum-exp.
+//  * The splits of a kv head form thread-block clusters. CTA c of a cluster owns
+//    output slice c: every CTA sends slice c of its (o, lse) partial into CTA c's
+//    shared memory with st.async (distributed shared memory, bytes counted by CTA c's
+//    mbarrier), and each CTA merges its slice once all contributions have landed: no
+//    cluster-wide barrier after the stage loops. When a kv head spans several
+//    clusters, each cluster slice is written to the caller's workspace and the last
+//    arriving CTA of that slice (release/acquire counter) merges the cluster partials
+//    by log-sum-exp.
 //  * Long sequences hand out their first eighth of stages one at a time (a per-kv-head
 //    ticket counter in the workspace) to the warps that finish their own range first.
 //  * Programmatic dependent launch (QIC_PDL): the CTA signals its dependents at
@@ -73,28 +74,20 @@ struct AttnShape {
   static constexpr int kFlagBytes = 64;
   static constexpr int kMlBytes = 2 * kConsumerWarps * 8 * 4;       // every warp's (m, l) per head column
   static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes + kMlBytes;
+  // the cluster merge's receive buffer follows (attn_rx_bytes, sized per launch)
+  static constexpr int kMaxRxBytes = (kMaxGroup * D + kMaxCluster * (kMaxGroup + 1)) * 4;
 };
+
+// Receive buffer of the cluster merge: one contribution per CTA of the cluster, each
+// a slice of ceil(G*D/C) outputs and the G per-head log-sum-exps padded to a multiple
+// of four (none for C = 1).
+__host__ __device__ constexpr int attn_rx_bytes(int G, int D, int C) {
+  return C > 1 ? C * ((G * D + C - 1) / C + ((G + 3) & ~3)) * 4 : 0;
+}
 
 __device__ __forceinline__ void consumer_sync() {
   __syncwarp();
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-}
-
-// Cluster barrier; every thread of every CTA in the cluster executes it the same
-// number of times (consumers and producers alike).
-// The non-.aligned form is used: each thread arrives on its own, so a warp that has
-// not reconverged after a divergent loop cannot complete the barrier early.
-__device__ __forceinline__ void cluster_sync_all() {
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Generic address of the same shared-memory variable in CTA `rank` of this cluster.
-template <typename X>
-__device__ __forceinline__ X* cluster_map(X* p, int rank) {
-  uint64_t out;
-  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
-  return reinterpret_cast<X*>(out);
 }
 
 __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* addr, int v) {
@@ -144,6 +137,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   volatile int* flags_s = reinterpret_cast<volatile int*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes);
   // [4][8] m then [4][8] l of the warps, written as each warp leaves its stage loop
   float* ml_s = reinterpret_cast<float*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes);
+  // the cluster merge: contributions of the cluster's CTAs to this CTA's output slice,
+  // and the mbarrier that counts their bytes (control slot 15; ring slots use 0-7)
+  float* rx = reinterpret_cast<float*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes +
+                                       Sh::kMlBytes);
+  uint64_t* rx_bar = full + 15;
   // flags_s[0]: abort, flags_s[1]: this CTA merges
 
   const int warp = threadIdx.x >> 5;
@@ -215,11 +213,23 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   if (threadIdx.x == 0) {
 #pragma unroll 1
     for (int i = 0; i < kRing; ++i) mbar_init(&full[i], 1);
+    if (p.cluster > 1) {
+      // bytes this CTA receives in the cluster merge: from each of the C CTAs, its
+      // share of this CTA's output slice and its G log-sum-exps
+      const int C = p.cluster, GD = G * D, sl = (GD + C - 1) / C, lo = (split % C) * sl;
+      const int cnt = max(0, min(GD, lo + sl) - lo);
+      const int nl = (sl % 4 == 0) ? ((G + 3) & ~3) : G;  // log-sum-exps sent (padded with 16-byte stores)
+      mbar_init(rx_bar, 1);
+      mbar_arrive_expect_tx(rx_bar, static_cast<uint32_t>(C * (cnt + nl) * 4));
+    }
     flags_s[0] = 0;
     flags_s[1] = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  // first cluster barrier phase: this CTA runs and its receive mbarrier is initialised
+  // (waited for just before the merge's first remote store)
+  if (p.cluster > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   pdl_launch_dependents();
 
   // ---- stage copies: every warp streams its own ring slots ----
@@ -682,17 +692,75 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     return;
   }
 
-  // ---- merge the partials of this cluster through distributed shared memory ----
-  cluster_sync_all();  // every CTA of the cluster has its partial in shared memory
+  // ---- merge the partials of this cluster: CTA c owns output slice c. Every CTA
+  // sends slice c of its partial, and its per-head log-sum-exps, into CTA c's receive
+  // buffer with st.async, then merges its own slice from its own shared memory once
+  // its mbarrier has counted all C contributions: no cluster-wide barrier, and no CTA
+  // waits at exit for its peers (its shared memory is only written, never read, by
+  // them, and every write to it has landed before it merges) ----
   const int C = p.cluster;
   const int rank = split % C;
   const int cid = split / C;
   const int nclust = nsplit / C;
-  // a kv head that is one cluster is past every stage loop: reset its ticket counter
-  if (nclust == 1 && rank == 0 && stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
   const int slice = (GD + C - 1) / C;
   const int lo = rank * slice;
   const int hi = min(GD, lo + slice);
+  const int Gp = (G + 3) & ~3;
+  const int rxs = slice + Gp;  // floats of one contribution in the receive buffer
+  consumer_sync();  // this CTA's partial is complete in `mine`
+  if (C > 1) {
+    // every CTA of the cluster runs and has initialised its receive mbarrier (the
+    // phase completed long ago; this orders nothing inside the CTA)
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+    if (slice % 4 == 0) {
+      // 16-byte stores (mine, the slices and the receive rows are 16-byte aligned);
+      // the log-sum-exp quads are padded with -inf
+      const int q4 = rxs / 4;
+#pragma unroll 1
+      for (int i = ctid; i < C * q4; i += kConsumerWarps * 32) {
+        const int c = i / q4, e = (i - c * q4) * 4;
+        float4 v;
+        if (e < slice) {
+          if (c * slice + e >= GD) continue;
+          v = aborted ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(mine + c * slice + e);
+        } else {
+          const int h = e - slice;
+          v.x = (!aborted && h < G) ? mine[GD + h] : -INFINITY;
+          v.y = (!aborted && h + 1 < G) ? mine[GD + h + 1] : -INFINITY;
+          v.z = (!aborted && h + 2 < G) ? mine[GD + h + 2] : -INFINITY;
+          v.w = (!aborted && h + 3 < G) ? mine[GD + h + 3] : -INFINITY;
+        }
+        st_async_cluster_f32x4(rx + rank * rxs + e, rx_bar, c, v);
+      }
+    } else {
+#pragma unroll 1
+      for (int i = ctid; i < C * (slice + G); i += kConsumerWarps * 32) {
+        const int c = i / (slice + G), e = i - c * (slice + G);
+        float v;
+        if (e < slice) {
+          if (c * slice + e >= GD) continue;
+          v = aborted ? 0.0f : mine[c * slice + e];
+        } else {
+          v = aborted ? -INFINITY : mine[GD + e - slice];  // an aborted CTA contributes nothing
+        }
+        st_async_cluster_f32(rx + rank * rxs + e, rx_bar, c, v);
+      }
+    }
+    // Bounded: a peer whose stage loop gave up at the deadline still sends, after
+    // draining its copies for at most one more timeout.
+    if (!mbar_wait(rx_bar, 0, deadline + 2 * p.timeout_ns)) {
+      if (ctid == 0) record_status(p.status, QIC_DEV_TIMEOUT);
+      return;
+    }
+  }
+  // a kv head that is one cluster is past every stage loop (each contribution is sent
+  // after its CTA's loop): reset its ticket counter
+  if (nclust == 1 && rank == 0 && stage_ctr != nullptr && ctid == 0) *stage_ctr = 0;
+  // contribution c: rx_o[c * rxs + idx - o_off] for output idx, rx_l[c * rxs + h] for
+  // head h (with one CTA per cluster, its own partial)
+  const float* rx_o = C > 1 ? rx : mine;
+  const float* rx_l = C > 1 ? rx + slice : mine + GD;
+  const int o_off = C > 1 ? lo : 0;
   // context parallel: this rank's merged slice (after the cross-cluster merge when the
   // kv head spans several clusters) goes to every rank as one contribution
   const int cpw = cp_slice_words(G, D);
@@ -713,13 +781,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
 #pragma unroll 1
   for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
     const int h = idx / D;
-    // all remote loads are issued before any is used: one DSMEM round trip
     float lse_c[kMaxCluster], o_c[kMaxCluster];
 #pragma unroll
     for (int c = 0; c < kMaxCluster; ++c) {
       if (c < C) {
-        lse_c[c] = *cluster_map(mine + GD + h, c);
-        o_c[c] = *cluster_map(mine + idx, c);
+        lse_c[c] = rx_l[c * rxs + h];
+        o_c[c] = rx_o[c * rxs + idx - o_off];
       }
     }
     float mx = -INFINITY;
@@ -746,11 +813,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
     }
   }
-  // This CTA's reads of its peers' partials are complete (their values are consumed
-  // above), so it tells the cluster with a relaxed arrive. The matching wait is the
-  // last thing before exit (shared memory must outlive the peers' reads), so the
-  // cross-cluster step below does not wait for the rest of the cluster.
-  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   if (nclust > 1) {
     // ---- merge the cluster partials of this slice: last arriving cluster ----
     consumer_sync();
@@ -870,7 +932,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       }
     }
   }
-  asm volatile("barrier.cluster.wait;" ::: "memory");
 }
 
 // ----------------------------------------------------------------------------
@@ -929,7 +990,7 @@ cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partial
 template <typename T, int D>
 static cudaError_t configure_typed() {
   static unsigned long long configured = 0;  // one bit per device ordinal
-  const int smem = AttnShape<D>::kSmemBytes;
+  const int smem = AttnShape<D>::kSmemBytes + AttnShape<D>::kMaxRxBytes;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -947,7 +1008,7 @@ static cudaError_t configure_typed() {
 
 template <typename T, int D>
 static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t stream) {
-  const int smem = AttnShape<D>::kSmemBytes;
+  const int smem = AttnShape<D>::kSmemBytes + attn_rx_bytes(p.G, D, p.cluster);
   cudaError_t e = configure_typed<T, D>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -971,13 +1032,16 @@ static cudaError_t launch_typed(const AttnParams& p, dim3 grid, cudaStream_t str
 }
 
 template <typename T, int D>
-static int max_active_clusters_typed(int cluster) {
-  // cached per device and cluster size: clusters of `cluster` CTAs that fit on the GPU at once
-  static int cache[64][kMaxCluster + 1] = {};
+static int max_active_clusters_typed(int cluster, int group) {
+  // cached per device, cluster size and query heads per kv head: clusters of `cluster`
+  // CTAs that fit on the GPU at once
+  static int cache[64][kMaxCluster + 1][kMaxGroup + 1] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || cluster < 1 || cluster > kMaxCluster) return 0;
-  if (cache[dev][cluster] != 0) return cache[dev][cluster];
-  const int smem = AttnShape<D>::kSmemBytes;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || cluster < 1 || cluster > kMaxCluster ||
+      group < 1 || group > kMaxGroup)
+    return 0;
+  if (cache[dev][cluster][group] != 0) return cache[dev][cluster][group];
+  const int smem = AttnShape<D>::kSmemBytes + attn_rx_bytes(group, D, cluster);
   if (configure_typed<T, D>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster, 1, 1);
@@ -995,22 +1059,22 @@ static int max_active_clusters_typed(int cluster) {
     cudaGetLastError();
     return 0;
   }
-  cache[dev][cluster] = n;
+  cache[dev][cluster][group] = n;
   return n;
 }
 
-int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster) {
+int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster, int group) {
   if (dtype == QIC_DTYPE_BF16) {
     switch (head_dim) {
-      case 64: return max_active_clusters_typed<__nv_bfloat16, 64>(cluster);
-      case 128: return max_active_clusters_typed<__nv_bfloat16, 128>(cluster);
-      case 256: return max_active_clusters_typed<__nv_bfloat16, 256>(cluster);
+      case 64: return max_active_clusters_typed<__nv_bfloat16, 64>(cluster, group);
+      case 128: return max_active_clusters_typed<__nv_bfloat16, 128>(cluster, group);
+      case 256: return max_active_clusters_typed<__nv_bfloat16, 256>(cluster, group);
     }
   } else {
     switch (head_dim) {
-      case 64: return max_active_clusters_typed<__half, 64>(cluster);
-      case 128: return max_active_clusters_typed<__half, 128>(cluster);
-      case 256: return max_active_clusters_typed<__half, 256>(cluster);
+      case 64: return max_active_clusters_typed<__half, 64>(cluster, group);
+      case 128: return max_active_clusters_typed<__half, 128>(cluster, group);
+      case 256: return max_active_clusters_typed<__half, 256>(cluster, group);
     }
   }
   return 0;

@@ -353,7 +353,7 @@ int launch_shape(const qic_decode_args* a, bool cp, int n_stages, int* n_splits_
     // us per layer; 8 chained d=256 S=32769 layers: 31.3 -> 30.2 us).
     const bool auto_cluster = cluster == 0;
     if (cluster == 0) cluster = 8;
-    int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster);
+    int max_clusters = qic::decode_attention_max_active_clusters(a->dtype, D, cluster, a->num_heads / Hkv);
     if (max_clusters <= 0) max_clusters = (3 * sm_count()) / cluster;  // three CTAs per SM
     if (a->flags & QIC_PDL) max_clusters = std::max(1, max_clusters * 5 / 6);
     // at most kMaxSplits splits per kv head: with one or two kv heads the wave is larger
@@ -615,7 +615,7 @@ int qic_batch_plan(const int32_t* seq_lens, int batch, int num_heads, int num_kv
   if (target_ctas <= 0) {
     // Whole waves of resident CTAs with at least ~1 MiB of K/V per work item (a CTA's
     // set-up and merge cost a few microseconds), at most 16 items per SM.
-    int resident = qic::decode_attention_max_active_clusters(QIC_DTYPE_BF16, head_dim, 1);
+    int resident = qic::decode_attention_max_active_clusters(QIC_DTYPE_BF16, head_dim, 1, num_heads / num_kv_heads);
     if (resident <= 0) resident = 3 * sm_count();
     const double bytes = static_cast<double>(total) * tok * head_dim * 2 * 2;
     const int max_waves = std::max(1, (16 * sm_count()) / resident);

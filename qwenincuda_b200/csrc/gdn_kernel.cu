@@ -18,8 +18,11 @@
 // share it (REP = Hv/Hk) times CB column blocks of the 128x128 fp32 state. Every CTA
 // of a cluster recomputes the 2x128 q/k conv channels from the old conv state; a
 // cluster barrier orders all those reads before any CTA writes the new conv state.
-// The gated RMSNorm needs the sum of squares over all 128 columns of a value head,
-// which the CB CTAs of that head exchange through distributed shared memory.
+// The gated RMSNorm needs the sum of squares over all 128 columns of a value head:
+// each of the CB CTAs of that head stores its partial into every peer's shared memory
+// with st.async, and each CTA waits on its own mbarrier for the CB partials (no
+// cluster-wide barrier at the end, whose release would wait for this CTA's state
+// stores to drain).
 //
 // Compiled without --use_fast_math: exp/log1p/sqrt follow the reference's host
 // arithmetic (std::exp, std::log1pf, std::sqrt), and the per-element multiply/add
@@ -36,6 +39,7 @@ namespace qic {
 constexpr int kGdnThreads = 128;
 constexpr int kGdnDk = 128;
 constexpr int kGdnDv = 128;
+constexpr uint64_t kGdnWaitNs = 2000000000ull;  // bound on the wait for the value head's peers
 
 template <typename T, int REP, int CB>
 __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_gdn_args a) {
@@ -67,6 +71,12 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   __shared__ __align__(16) float delta_s[NC];
   __shared__ float col_s[NC];
   __shared__ float ssq_all[CB];  // the value head's CB partial sums of squares, pushed by their CTAs
+  __shared__ __align__(8) uint64_t ssq_bar;  // completes when all CB partials have landed in ssq_all
+  if (tid == 0) {
+    mbar_init(&ssq_bar, 1);
+    mbar_arrive_expect_tx(&ssq_bar, CB * 4);
+    fence_mbar_init();  // visible to the peers' st.async after the cluster barrier's first phase
+  }
 
   const T* qkv = static_cast<const T*>(a.qkv);
   const T* conv_w = static_cast<const T*>(a.conv_w);
@@ -261,12 +271,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     ss_mine = ss;
   }
-  // every CTA of the cluster is running and has read the old conv state
+  // every CTA of the cluster is running, has initialised its mbarrier and has read
+  // the old conv state
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-  // this CTA's partial goes into slot cb of every CTA of its value head (DSMEM stores
-  // before the cluster barrier below), so after that barrier every CTA reads only its
-  // own shared memory and may exit without waiting for its peers
-  if (tid < CB) *cluster.map_shared_rank(&ssq_all[cb], vloc * CB + tid) = ss_mine;
+  // this CTA's partial goes into slot cb of every CTA of its value head; each CTA
+  // reads only its own shared memory once its mbarrier shows all CB slots written, so
+  // no CTA waits at exit for its peers
+  if (tid < CB) st_async_cluster_f32(&ssq_all[cb], &ssq_bar, vloc * CB + tid, ss_mine);
   // the new conv state (q/k channels by the first value head's CTAs, v channels by
   // their owner)
   if (vloc == 0) {
@@ -287,19 +298,23 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
       if (t < K) conv_state[static_cast<size_t>(cv) * K + t] = win_v[t];
     }
   }
-  cluster.sync();  // every partial of this value head is in ssq_all
+  if (tid >= NC) return;
+  // every partial of this value head is in ssq_all (bounded wait: the peers of a
+  // cluster run together, so only a broken launch gives up)
+  if (!mbar_wait(&ssq_bar, 0, globaltimer_ns() + kGdnWaitNs)) {
+    if (a.status != nullptr) record_status(a.status, QIC_DEV_TIMEOUT);
+    return;
+  }
   float ss = 0.0f;
 #pragma unroll
   for (int c = 0; c < CB; ++c) ss += ssq_all[c];
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kGdnDv) + a.eps);
-  if (tid < NC) {
-    const int j = cb * NC + tid;
-    const float normed = __fmul_rn(col_s[tid], inv);
-    const float zv = to_f32<T>(z_raw);
-    const float gate = zv / (1.0f + expf(-zv));
-    const float ww = to_f32<T>(nw_raw);
-    static_cast<T*>(a.out)[static_cast<size_t>(vh) * kGdnDv + j] = from_f32<T>(__fmul_rn(__fmul_rn(normed, ww), gate));
-  }
+  const int j = cb * NC + tid;
+  const float normed = __fmul_rn(col_s[tid], inv);
+  const float zv = to_f32<T>(z_raw);
+  const float gate = zv / (1.0f + expf(-zv));
+  const float ww = to_f32<T>(nw_raw);
+  static_cast<T*>(a.out)[static_cast<size_t>(vh) * kGdnDv + j] = from_f32<T>(__fmul_rn(__fmul_rn(normed, ww), gate));
 }
 
 template <typename T, int REP, int CB>

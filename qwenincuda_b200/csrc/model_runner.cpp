@@ -61,7 +61,7 @@ struct qic_model {
   void* logits = nullptr;   // [vocab]
   void* ws = nullptr;       // attention workspace
   size_t ws_bytes = 0;
-  int32_t* dev_scalars = nullptr;  // [0] token, [1] sequence length, [2] greedy token, [3] GEMV status
+  int32_t* dev_scalars = nullptr;  // [0] token, [1] sequence length, [2] greedy token, [3] GEMV / GatedDeltaNet status
   int32_t* host_scalars = nullptr; // pinned: dev_scalars[0..3], then the attention workspace's status word
   std::vector<void*> k_cache, v_cache;               // per layer ([max_seq_len, kv_dim]) or null
   std::vector<float*> conv_state, recurrent_state;   // per layer or null
@@ -224,6 +224,7 @@ int record_step(qic_model* m, cudaStream_t s) {
       g.conv_state = m->conv_state[i];
       g.recurrent_state = m->recurrent_state[i];
       g.out = m->lout;
+      g.status = gemv_status;  // a bounded wait's timeout, reported like the GEMV's
       rc = qic_gated_delta_decode(&g, st);
       if (rc != QIC_SUCCESS) break;
       rc = gemv(m->lout, static_cast<int>(d.val_dim), QIC_GEMV_RESIDUAL, nullptr,

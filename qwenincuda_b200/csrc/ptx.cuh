@@ -67,6 +67,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// 32-bit store into the same shared-memory variable of CTA `rank` of this cluster
+// (st.async), completing 4 bytes on that CTA's mbarrier at `local_bar`'s offset: the
+// receiver learns of it by waiting on its own mbarrier, with no cluster-wide barrier
+// and no fence over this CTA's earlier global stores.
+__device__ __forceinline__ void st_async_cluster_f32(const float* local_dst, const uint64_t* local_bar, int rank,
+                                                     float v) {
+  uint32_t dst, bar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(local_dst)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_u32(local_bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
+}
+
+// The same for four floats (16 bytes; `local_dst` 16-byte aligned): one store and one
+// mbarrier update for four values.
+__device__ __forceinline__ void st_async_cluster_f32x4(const float* local_dst, const uint64_t* local_bar, int rank,
+                                                       float4 v) {
+  uint32_t dst, bar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(local_dst)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_u32(local_bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   dst),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(bar)
+               : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
 // ----------------------------------------------------------------------------

@@ -154,7 +154,7 @@ cudaError_t launch_decode_attention(int dtype, int head_dim, const AttnParams& p
 cudaError_t launch_attention_merge(int dtype, int head_dim, const float* partials, int n, int H, int Hkv,
                                    const void* gate, void* out, cudaStream_t stream);
 // Clusters of `cluster` CTAs of the decode kernel that can be resident at once (0 if unknown).
-int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster);
+int decode_attention_max_active_clusters(int dtype, int head_dim, int cluster, int group);
 
 // Standalone ops (rowops.cu)
 cudaError_t launch_head_rmsnorm(int dtype, const void* x, const void* w, int num_heads, int head_dim, float eps,

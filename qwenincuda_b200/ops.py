@@ -217,8 +217,9 @@ def launch_paged_attention(q, k_cache, v_cache, page_table, page_size, num_heads
 
 def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, out,
                        num_k_heads, num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6,
-                       pdl=False, stream=None):
-    """One GatedDeltaNet decode step; conv_state and recurrent_state (fp32) are updated in place."""
+                       pdl=False, status=None, stream=None):
+    """One GatedDeltaNet decode step; conv_state and recurrent_state (fp32) are updated in place.
+    status: an optional CUDA int32 tensor whose first word collects QIC_DEV_TIMEOUT."""
     g = GdnArgs()
     g.flags = QIC_PDL if pdl else 0
     g.dtype = dtype_code(qkv)
@@ -231,6 +232,7 @@ def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_sta
     g.qkv, g.z, g.b, g.a = _ptr(qkv), _ptr(z), _ptr(b), _ptr(a)
     g.conv_w, g.dt_bias, g.a_log, g.norm_w = _ptr(conv_w), _ptr(dt_bias), _ptr(a_log), _ptr(norm_w)
     g.conv_state, g.recurrent_state, g.out = _ptr(conv_state), _ptr(recurrent_state), _ptr(out)
+    g.status = _ptr(status)
     check(lib().qic_gated_delta_decode(ctypes.byref(g), _stream(stream)), "qic_gated_delta_decode")
 
 

@@ -75,6 +75,55 @@ def test_noalloc_takes_no_device_memory():
     assert _noalloc_status(L, stream) == 0
 
 
+def test_noalloc_graph_replays_a_chained_decode_loop():
+    """Two noalloc calls (two layers, chained with QIC_PDL, the length read from device
+    memory) captured once in a CUDA graph and replayed at three lengths give the bytes
+    of the workspace entry point called with each length by value, at the same launch
+    shape; the scratch status word stays clear."""
+    L = q.lib()
+    S_max = 5000
+    cfg = AttnConfig("noalloc_graph", 32, 8, 128, S_max, layers=2, seed=25)
+    inp = make_attention_inputs(cfg, paged=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    shape = dict(num_splits=16, cluster_size=8, deterministic=True)
+
+    def call(layer, out, seq_len, entry, **kw):
+        a = q.ops.decode_args(
+            q=inp.q[layer], k_cache=inp.k_cache[layer], v_cache=inp.v_cache[layer], out=out,
+            num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, seq_len=seq_len,
+            page_table=inp.page_table[layer], page_size=cfg.page_size, cache_tokens=inp.cache_tokens, **shape, **kw)
+        assert entry(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+
+    lengths = (4999, 3001, 17)
+    ws = q.Workspace(cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, S_max)
+    want = []
+    for S in lengths:
+        outs = [torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        for layer in range(2):
+            call(layer, outs[layer], S, L.qic_decode_attention, workspace=ws)
+        want.append(outs)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+
+    length = torch.tensor([S_max], dtype=torch.int32, device="cuda")
+    outs = [torch.empty(cfg.num_heads * cfg.head_dim, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    for layer in range(2):  # the first call on a device looks up the scratch: outside the capture
+        call(layer, outs[layer], S_max, L.qic_decode_attention_noalloc, pdl=True, seq_len_dev=length)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for layer in range(2):
+            call(layer, outs[layer], S_max, L.qic_decode_attention_noalloc, pdl=True, seq_len_dev=length)
+    for t, S in enumerate(lengths):
+        length.fill_(S)
+        graph.replay()
+        torch.cuda.synchronize()
+        for layer in range(2):
+            assert torch.equal(outs[layer].view(torch.int16), want[t][layer].view(torch.int16)), f"S={S} layer {layer}"
+    assert _noalloc_status(L, stream) == 0
+    del graph
+
+
 def test_noalloc_reports_a_bad_page_entry():
     """A page-table entry outside the cache is clamped by the kernel's bounds check and
     its bit stays in the array's status word, through a later clean call, until
