@@ -314,7 +314,10 @@ def gdn_workload(layers=GDN_STACK_LAYERS):
         g.dtype = 1
         g.num_k_heads, g.num_v_heads, g.k_head_dim, g.v_head_dim = cfg.num_k_heads, cfg.num_v_heads, 128, 128
         g.conv_kernel, g.eps = cfg.conv_kernel, cfg.eps
-        g.flags = q.abi.QIC_PDL  # the next layer may start its weight loads and prefetches while this one runs
+        # the next layer may start its weight and state loads while this one runs: each
+        # layer's states are written once per step, and every step is its own graph
+        # launch, so their writer has completed before the launch starts
+        g.flags = q.abi.QIC_PDL | q.abi.QIC_GDN_STATES_READY
         for k in ("qkv", "z", "b", "a", "conv_w", "dt_bias", "a_log", "norm_w", "conv_state", "recurrent_state",
                   "out"):
             setattr(g, k, t[k].data_ptr())

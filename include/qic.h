@@ -403,7 +403,9 @@ typedef struct qic_gdn_args {
                                loading the weights (conv_w, dt_bias, a_log, norm_w, which no kernel
                                may write meanwhile) and prefetching the states into L2; the states
                                and qkv, z, b, a are read after that kernel has completed. The
-                               kernel always lets the next kernel in the stream start early. */
+                               kernel always lets the next kernel in the stream start early.
+                               QIC_GDN_STATES_READY (with QIC_PDL): the states are read, not only
+                               prefetched, before that point (see below). */
   const void* qkv;          /* [2*Hk*dk + Hv*dv] in_proj_qkv output (conv input) */
   const void* z;            /* [Hv*dv] */
   const void* b;            /* [Hv] */
@@ -419,6 +421,17 @@ typedef struct qic_gdn_args {
                                CTA gives up waiting for its value head's peers (the output of that
                                head is then not written) */
 } qic_gdn_args;
+
+/* Flag of qic_gdn_args.flags. The caller guarantees that every kernel which wrote
+ * conv_state or recurrent_state has completed before this launch starts, so with QIC_PDL
+ * the kernel reads them before waiting for the previous kernel (only the step's inputs
+ * qkv, z, b, a are read after it). This holds when a stream operation without
+ * programmatic dependent launch lies between the states' last writer and this launch: a
+ * copy, a kernel launched without QIC_PDL, or the boundary between two CUDA graph
+ * launches (a layer stack captured as one graph per decode step, each layer's states
+ * written once per step). It does not hold for two PDL launches of the same layer
+ * back to back. */
+#define QIC_GDN_STATES_READY 256u
 
 /* One decode step of src/model.cpp:692-791 on the device: conv-state shift and causal
  * conv + SiLU, L2-norm of q/k, head repeat, beta/g gates, delta-rule state update and

@@ -20,6 +20,7 @@ QIC_EXPLICIT_POSITION = 16
 QIC_DETERMINISTIC = 32
 QIC_Q_GATE_INTERLEAVED = 64
 QIC_DEVICE_SEQ_LEN = 128
+QIC_GDN_STATES_READY = 256
 QIC_MAX_RANKS = 8
 QIC_MAX_SEQ_LEN = 1 << 30
 QIC_IPC_HANDLE_BYTES = 64

@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   // The states may be written by an earlier kernel that is still running (with
   // programmatic dependent launch a kernel further back in the stream can be, e.g.
   // this layer's previous step): before the wait they are only prefetched into L2,
-  // the point of coherence, and read after it together with the step's inputs ----
+  // the point of coherence, and read after it together with the step's inputs, unless
+  // the caller guarantees their writer has completed (QIC_GDN_STATES_READY) ----
   const int quad = tid % QUADS;
   const int rg = tid / QUADS;
   float* state = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv + cb * NC + quad * 4;
@@ -96,17 +97,39 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   const int cq = kh * kGdnDk + tid;
   const int ck = Hk * kGdnDk + kh * kGdnDk + tid;
   const int cv = 2 * Hk * kGdnDk + vh * kGdnDv + cb * NC + tid;
-  // row `tid` of this CTA's state block (NC columns: one or two lines) and the three
-  // conv windows
-  {
+  // With QIC_GDN_STATES_READY the caller guarantees that the states' last writer has
+  // completed, so they are read here; otherwise row `tid` of this CTA's state block (NC
+  // columns: one or two lines) and the three conv windows are prefetched.
+  const bool states_ready = (a.flags & QIC_GDN_STATES_READY) != 0;
+  float4 s[RPT];
+  // win: the channel's new window [old[1..K-1], x] (x is filled in after the wait)
+  float win_q[8], win_k[8], win_v[8];
+  auto load_state = [&]() {
+#pragma unroll
+    for (int r = 0; r < RPT; ++r)
+      s[r] = *reinterpret_cast<const float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv);
+  };
+  auto load_window = [&](int c, float (&win)[8]) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) win[t] = (t < K - 1) ? conv_state[static_cast<size_t>(c) * K + t + 1] : 0.0f;
+  };
+  auto load_windows = [&]() {
+    load_window(cq, win_q);
+    load_window(ck, win_k);
+    if (tid < NC) load_window(cv, win_v);
+  };
+  if (states_ready) {
+    load_state();
+    load_windows();
+  } else {
     const float* row = a.recurrent_state + static_cast<size_t>(vh) * kGdnDk * kGdnDv +
                        static_cast<size_t>(tid) * kGdnDv + cb * NC;
 #pragma unroll
     for (int c = 0; c < NC; c += 32) prefetch_l2(row + c);
+    prefetch_l2(conv_state + static_cast<size_t>(cq) * K);
+    prefetch_l2(conv_state + static_cast<size_t>(ck) * K);
+    if (tid < NC) prefetch_l2(conv_state + static_cast<size_t>(cv) * K);
   }
-  prefetch_l2(conv_state + static_cast<size_t>(cq) * K);
-  prefetch_l2(conv_state + static_cast<size_t>(ck) * K);
-  if (tid < NC) prefetch_l2(conv_state + static_cast<size_t>(cv) * K);
   const T dt_raw = static_cast<const T*>(a.dt_bias)[vh];
   const T al_raw = static_cast<const T*>(a.a_log)[vh];
   T nw_raw = T();
@@ -121,23 +144,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   if (tid < NC) taps(cv, wt_v);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  float4 s[RPT];
-#pragma unroll
-  for (int r = 0; r < RPT; ++r) s[r] = *reinterpret_cast<const float4*>(state + static_cast<size_t>(rg + RG * r) * kGdnDv);
+  if (!states_ready) {
+    load_state();
+    load_windows();
+  }
   const T bv_raw = static_cast<const T*>(a.b)[vh];
   const T av_raw = static_cast<const T*>(a.a)[vh];
   T z_raw = T();
   if (tid < NC) z_raw = static_cast<const T*>(a.z)[static_cast<size_t>(vh) * kGdnDv + cb * NC + tid];
 
   // ---- 1. causal conv + SiLU from the old conv state ----
-  // win: the channel's new window [old[1..K-1], x]
-  float win_q[8], win_k[8], win_v[8];
   auto conv_channel = [&](int c, float (&win)[8], const T (&wt)[8]) -> float {
     const float x = to_f32<T>(qkv[c]);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      win[t] = (t < K - 1) ? conv_state[static_cast<size_t>(c) * K + t + 1] : ((t == K - 1) ? x : 0.0f);
-    }
+    for (int t = 0; t < 8; ++t)
+      if (t == K - 1) win[t] = x;
     float acc = 0.0f;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
@@ -235,6 +256,15 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   const float inv_k = 1.0f / sqrtf(sk + 1e-6f);
   const float qscale = __fmul_rn(inv_q, 1.0f / sqrtf(static_cast<float>(kGdnDk)));
   const float kq = __fmul_rn(__fmul_rn(sqk, inv_k), qscale);  // k^ . q^
+  // Warp 0 sends this CTA's sum of squares into slot cb of every CTA of its value head
+  // (after the cluster barrier's first phase: every CTA runs, has initialised its
+  // mbarrier and has read the old conv state); each CTA then reads only its own shared
+  // memory once its mbarrier shows all CB slots written, so no CTA waits at exit for
+  // its peers.
+  auto push_ssq = [&](float ss) {
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+    if (tid < CB) st_async_cluster_f32(&ssq_all[cb], &ssq_bar, vloc * CB + tid, ss);
+  };
   if (tid < NC) {
     float cq_sum = 0.0f, ck_sum = 0.0f;
 #pragma unroll
@@ -245,7 +275,16 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
     const float kv_mem = __fmul_rn(ck_sum, inv_k);
     const float delta = __fmul_rn(v_s[tid] - kv_mem, beta);
     delta_s[tid] = delta;
-    col_s[tid] = __fadd_rn(__fmul_rn(cq_sum, qscale), __fmul_rn(kq, delta));  // o
+    const float o = __fadd_rn(__fmul_rn(cq_sum, qscale), __fmul_rn(kq, delta));
+    col_s[tid] = o;
+    if constexpr (NC == 32) {
+      // warp 0 holds all of this CTA's columns: its sum of squares goes to the value
+      // head's CTAs now, ahead of the state update
+      float ss = __fmul_rn(o, o);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      push_ssq(ss);
+    }
   }
   __syncthreads();
   // the new state: S' = S_g + k^ delta^T
@@ -263,21 +302,18 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
   }
 
   // ---- 6. gated RMSNorm over the value head's 128 columns (src/model.cpp:777-791) ----
-  float ss_mine = 0.0f;  // this CTA's sum of squares (warp 0)
-  if (tid < 32) {
-    float ss = 0.0f;
-    for (int j = tid; j < NC; j += 32) ss = __fadd_rn(ss, __fmul_rn(col_s[j], col_s[j]));
+  if constexpr (NC != 32) {
+    float ss = 0.0f;  // this CTA's sum of squares (warp 0)
+    if (tid < 32) {
+      for (int j = tid; j < NC; j += 32) ss = __fadd_rn(ss, __fmul_rn(col_s[j], col_s[j]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    ss_mine = ss;
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      push_ssq(ss);
+    }
   }
-  // every CTA of the cluster is running, has initialised its mbarrier and has read
-  // the old conv state
-  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-  // this CTA's partial goes into slot cb of every CTA of its value head; each CTA
-  // reads only its own shared memory once its mbarrier shows all CB slots written, so
-  // no CTA waits at exit for its peers
-  if (tid < CB) st_async_cluster_f32(&ssq_all[cb], &ssq_bar, vloc * CB + tid, ss_mine);
+  // the threads that did not send a partial: every CTA of the cluster has read the old
+  // conv state before any conv-state write below
+  if (tid >= 32) asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
   // the new conv state (q/k channels by the first value head's CTAs, v channels by
   // their owner)
   if (vloc == 0) {

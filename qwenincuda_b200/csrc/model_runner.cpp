@@ -212,7 +212,10 @@ int record_step(qic_model* m, cudaStream_t s) {
       g.v_head_dim = c.linear_value_head_dim;
       g.conv_kernel = c.linear_conv_kernel_dim;
       g.eps = c.rms_norm_eps;
-      g.flags = QIC_PDL;
+      // each layer's states are written once per step and every step is its own graph
+      // launch (or the eager first step after the states were cleared), so their writer
+      // has completed before this launch starts
+      g.flags = QIC_PDL | QIC_GDN_STATES_READY;
       g.qkv = m->lqkv;
       g.z = m->lz;
       g.b = m->lb;

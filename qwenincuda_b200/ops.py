@@ -18,6 +18,7 @@ from .abi import (
     QIC_DTYPE_F16,
     QIC_DETERMINISTIC,
     QIC_DEVICE_SEQ_LEN,
+    QIC_GDN_STATES_READY,
     QIC_EXPLICIT_POSITION,
     QIC_FUSE_APPEND,
     QIC_FUSE_Q_PROLOGUE,
@@ -217,11 +218,13 @@ def launch_paged_attention(q, k_cache, v_cache, page_table, page_size, num_heads
 
 def gated_delta_decode(*, qkv, z, b, a, conv_w, dt_bias, a_log, norm_w, conv_state, recurrent_state, out,
                        num_k_heads, num_v_heads, k_head_dim=128, v_head_dim=128, conv_kernel=4, eps=1e-6,
-                       pdl=False, status=None, stream=None):
+                       pdl=False, states_ready=False, status=None, stream=None):
     """One GatedDeltaNet decode step; conv_state and recurrent_state (fp32) are updated in place.
+    states_ready (with pdl): QIC_GDN_STATES_READY, the caller guarantees that the kernels
+    which last wrote the states have completed before this launch starts.
     status: an optional CUDA int32 tensor whose first word collects QIC_DEV_TIMEOUT."""
     g = GdnArgs()
-    g.flags = QIC_PDL if pdl else 0
+    g.flags = (QIC_PDL if pdl else 0) | (QIC_GDN_STATES_READY if states_ready else 0)
     g.dtype = dtype_code(qkv)
     g.num_k_heads = num_k_heads
     g.num_v_heads = num_v_heads

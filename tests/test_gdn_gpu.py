@@ -65,6 +65,45 @@ def test_gdn_pdl_chain_matches_plain_launches(layers):
             assert torch.equal(x, y), f"layer {l} {name}"
 
 
+def test_gdn_states_ready_graph_matches_plain_launches():
+    """A stack of four GatedDeltaNet layers captured once as a CUDA graph with
+    QIC_PDL | QIC_GDN_STATES_READY (the states read before griddepcontrol.wait: each
+    layer's states are written once per replay, and replays are whole graph launches)
+    and replayed three times gives the bytes of three rounds of plain launches."""
+    import dataclasses
+
+    def stack():
+        return [make_gdn_inputs(dataclasses.replace(GdnConfig(), seed=200 + l)) for l in range(4)]
+
+    def step(st, **kw):
+        for l, t in enumerate(st):
+            z = t["z"] if l == 0 else st[l - 1]["out"]
+            q.gated_delta_decode(qkv=t["qkv"], z=z, b=t["b"], a=t["a"], conv_w=t["conv_w"], dt_bias=t["dt_bias"],
+                                 a_log=t["a_log"], norm_w=t["norm_w"], conv_state=t["conv_state"],
+                                 recurrent_state=t["recurrent_state"], out=t["out"], num_k_heads=16, num_v_heads=32,
+                                 **kw)
+
+    plain = stack()
+    for _ in range(3):
+        step(plain)
+    torch.cuda.synchronize()
+    fast = stack()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step(fast, pdl=True, states_ready=True, status=status)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for l, (x, y) in enumerate(zip(plain, fast)):
+        for name in ("out", "conv_state", "recurrent_state"):
+            assert torch.equal(x[name], y[name]), f"layer {l} {name}"
+    del graph
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_gdn_kernel_vs_reference_step(dtype):
     """The CUDA kernel against the reference's own decode step (run_linear_attention_block,
