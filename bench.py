@@ -228,11 +228,15 @@ def _call(fn, args_struct):
 # workloads: each returns dict(step=callable, bytes=int, launches=int per step,
 # e2e=(callable, h2d, d2h), kernel=name, status=callable, config=dict)
 # ---------------------------------------------------------------------------
-def attention_workload(name, layout, layers=None, splits=0):
+def attention_workload(name, layout, layers=None, splits=0, seq_len=None):
+    import dataclasses
+
     import qwenincuda_b200 as q
     from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
 
     cfg = CONFIGS[name]
+    if seq_len:
+        cfg = dataclasses.replace(cfg, seq_len=seq_len)
     inp = make_attention_inputs(cfg, paged=(layout == "paged"), layers=layers)
     L_ = inp.q.shape[0]
     # the step's per-layer inputs (q, k_new, v_new of every layer) live in one device
@@ -1126,6 +1130,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="only the requested workload (profiling runs)")
     ap.add_argument("--splits", type=int, default=0, help="attention splits per kv head (tuning runs; 0 = chosen)")
+    ap.add_argument("--seq-len", type=int, default=0, help="attended tokens of an attention workload (tuning runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
@@ -1146,7 +1151,7 @@ def main():
         if "allgather_nccl_path" in res:
             extra["allgather_nccl_path"] = res["allgather_nccl_path"]
     elif args.workload in ATTN_WORKLOADS:
-        wl = attention_workload(args.workload, "paged", args.layers, args.splits)
+        wl = attention_workload(args.workload, "paged", args.layers, args.splits, args.seq_len)
         ms, ms_e2e, clocks = measure(wl, args, world, local)
         if world == 1 and not args.no_extra:
             extra["e2e_eager"] = eager_e2e(wl, args)

@@ -73,7 +73,8 @@ struct AttnShape {
   static constexpr int kQBytes = kMaxGroup * D * 2;
   static constexpr int kFlagBytes = 64;
   static constexpr int kMlBytes = 2 * kConsumerWarps * 8 * 4;       // every warp's (m, l) per head column
-  static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes + kMlBytes;
+  static constexpr int kAppBytes = 2 * D * 2;                         // the appended k and v rows
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kCtrlBytes + kQBytes + kFlagBytes + kMlBytes + kAppBytes;
   // the cluster merge's receive buffer follows (attn_rx_bytes, sized per launch)
   static constexpr int kMaxRxBytes = (kMaxGroup * D + kMaxCluster * (kMaxGroup + 1)) * 4;
 };
@@ -139,16 +140,22 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   float* ml_s = reinterpret_cast<float*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes);
   // the cluster merge: contributions of the cluster's CTAs to this CTA's output slice,
   // and the mbarrier that counts their bytes (control slot 15; ring slots use 0-7)
+  // the appended k row then v row, as stored into the cache
+  T* app_s = reinterpret_cast<T*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes + Sh::kMlBytes);
   float* rx = reinterpret_cast<float*>(ring + Sh::kRingBytes + Sh::kCtrlBytes + Sh::kQBytes + Sh::kFlagBytes +
-                                       Sh::kMlBytes);
+                                       Sh::kMlBytes + Sh::kAppBytes);
   uint64_t* rx_bar = full + 15;
-  // flags_s[0]: abort, flags_s[1]: this CTA merges
+  // flags_s[0]: abort, flags_s[1]: this CTA merges, flags_s[2]: app_s holds the append
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   // ---- this CTA's unit of work ----
   int b, kvh, split, nsplit, st_lo, st_hi, S, part_base;
+  // Single-sequence launches whose appended token is alone in the sequence's last stage
+  // (S - 1 a multiple of the stage size: positions 2^k, for instance) take that token's
+  // contribution from the appending warp's registers and never copy the stage.
+  bool tail_regs = false;
   if (p.plan != nullptr) {
     const WorkItem w = p.plan[blockIdx.x];
     b = w.b;
@@ -165,7 +172,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     split = blockIdx.x;
     nsplit = p.n_splits;
     S = p.seq_len;
-    int nst = p.n_stages;
     if (p.seq_len_dev != nullptr) {
       // the current length, written before this launch like the page table; the launch
       // is sized for p.seq_len, so a length outside [1, p.seq_len] is clamped into it
@@ -175,8 +181,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         sd = sd < 1 ? 1 : p.seq_len;
       }
       S = sd;
-      nst = (S + TOK - 1) / TOK;
     }
+    tail_regs = (p.flags & QIC_FUSE_APPEND) && S > 1 && (S - 1) % TOK == 0;
+    const int nst = (S + TOK - 1) / TOK - (tail_regs ? 1 : 0);  // stages copied
     st_lo = static_cast<int>(static_cast<long long>(split) * nst / nsplit);
     st_hi = static_cast<int>(static_cast<long long>(split + 1) * nst / nsplit);
     part_base = kvh * (nsplit / p.cluster);  // one global slot per cluster
@@ -189,6 +196,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     return;
   }
   const int n_stages_seq = (S + TOK - 1) / TOK;
+  const int n_copy = n_stages_seq - (tail_regs ? 1 : 0);  // stages that go through the ring
   // Stages of this CTA (absolute indices in the sequence): its own contiguous range
   // [a0, a1), and, in single-sequence launches with a workspace and at least 8
   // stages per split, a share of the first eighth of the sequence, [0, pool_n),
@@ -198,15 +206,15 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   // Batched work items keep their planned range.
   int a0 = st_lo, a1 = st_hi, pool_n = 0;
   int* stage_ctr = nullptr;
-  if (p.plan == nullptr && p.stage_ctr != nullptr && n_stages_seq >= 8 * nsplit) {
-    pool_n = n_stages_seq / 8;
-    const int rest = n_stages_seq - pool_n;
+  if (p.plan == nullptr && p.stage_ctr != nullptr && n_copy >= 8 * nsplit) {
+    pool_n = n_copy / 8;
+    const int rest = n_copy - pool_n;
     a0 = pool_n + static_cast<int>(static_cast<long long>(split) * rest / nsplit);
     a1 = pool_n + static_cast<int>(static_cast<long long>(split + 1) * rest / nsplit);
     stage_ctr = p.stage_ctr + kvh;
   }
   const int G = p.G;
-  const bool do_append = (p.flags & QIC_FUSE_APPEND) && a1 == n_stages_seq && a1 > a0;
+  const bool do_append = (p.flags & QIC_FUSE_APPEND) && a1 == n_copy && a1 > a0;
   const int32_t* table = p.page_table != nullptr ? p.page_table + static_cast<size_t>(b) * p.table_bstride : nullptr;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
 
@@ -224,6 +232,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     flags_s[0] = 0;
     flags_s[1] = 0;
+    flags_s[2] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -251,7 +260,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int bx = lane & 15;
   const CUtensorMap* tmap = lane < 16 ? &p.tm_k : &p.tm_v;
   const int kv_off = lane < 16 ? 0 : Sh::kKBytes;
-  const int append_stage = do_append ? n_stages_seq - 1 : -1;
+  const int append_stage = (do_append && !tail_regs) ? n_stages_seq - 1 : -1;  // copied stage holding it
   // page-table entry holding box bx of stage j, or -1
   auto box_entry = [&](int j) -> int {
     const int tb = j * TOK + bx * bh;
@@ -282,8 +291,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   };
   // cur[k]: stage in this warp's k-th slot (issued, not yet consumed) or -1
   int cur[kSlots], lap[kSlots];
-  int deferred = -1;  // own slot whose stage waits for the append
-  int live = 0;       // slots holding a stage
+  int live = 0;  // slots holding a stage
 #pragma unroll
   for (int k = 0; k < kSlots; ++k) {
     const int j = a0 + warp + k * kConsumerWarps;
@@ -291,22 +299,21 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     lap[k] = 0;
     live += cur[k] >= 0 ? 1 : 0;
   }
-  // initial fill, before the inputs of the preceding kernel are waited for; the stage
-  // holding the appended token waits for the append. pg_st[k]: page-table entry of
-  // the slot's next own stage (cur[k] + kRing), loaded one stage ahead.
+  // initial fill, before the inputs of the preceding kernel are waited for. The stage
+  // holding the appended token is copied too, with the row's old bytes: its consumer
+  // overwrites that row in shared memory with the appended k and v rows (app_s) before
+  // using it, so the append's global write is not waited for by a copy. pg_st[k]:
+  // page-table entry of the slot's next own stage (cur[k] + kRing), loaded one stage
+  // ahead.
   int pg_st[kSlots];
-  int pg_def = 0;  // page-table entry of the deferred stage
+  bool app_patch = false;  // this warp copied the stage holding the appended row before the append
 #pragma unroll
   for (int k = 0; k < kSlots; ++k) {
     pg_st[k] = 0;
     if (cur[k] < 0) continue;
     const int pg0 = table != nullptr ? load_entry(box_entry(cur[k])) : 0;
     if (table != nullptr && cur[k] + kRing < a1) pg_st[k] = load_entry(box_entry(cur[k] + kRing));
-    if (cur[k] == append_stage) {
-      deferred = k;
-      pg_def = pg0;
-      continue;
-    }
+    if (cur[k] == append_stage) app_patch = true;
     issue(cur[k], pg0, warp + k * kConsumerWarps);
   }
   // Measured and not kept: also prefetching each slot's next 1 / 2 / 4 own stages
@@ -377,20 +384,20 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         const size_t at = static_cast<size_t>(app_slot) * static_cast<size_t>(p.Hkv) * D + static_cast<size_t>(kvh) * D;
         row_store<T, D>(static_cast<T*>(p.k_cache) + at, kr, lane);
         row_store<T, D>(static_cast<T*>(p.v_cache) + at, vr, lane);
+        // the same bytes for the consumer of the stage holding this row
+        row_store<T, D>(app_s, kr, lane);
+        row_store<T, D>(app_s + D, vr, lane);
+        if (lane == 0) flags_s[2] = 1;
       } else if (lane == 0) {
         record_status(p.status, QIC_DEV_BAD_PAGE);
       }
-      // the stage holding this row is copied by TMA (async proxy) after the barrier below
+      // a later copy of this row (a stage issued after the barrier below) goes through
+      // TMA, the async proxy
       fence_proxy_async_global();
       __syncwarp();
     }
   }
   consumer_sync();
-  // the rest of the initial fill: the stage holding the appended token
-  if (deferred >= 0) {
-    fence_proxy_async_global();
-    issue(cur[deferred], pg_def, warp + deferred * kConsumerWarps);
-  }
   // Tickets of the pool: a warp asks for its next stage when it issues one, and
   // reads the answer (and starts loading that stage's page-table entries) when it
   // begins the following stage, so the atomic and the table load overlap compute.
@@ -445,6 +452,40 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   const float sl2 = p.scale_log2;
   bool ok = true;
+  if (tail_regs && do_append && warp == G % kConsumerWarps && flags_s[2] != 0) {
+    // the appended token, alone in the uncopied last stage: this warp's softmax state
+    // starts from it (score against each q row, l = 1, o = its v row), with its k and
+    // v rows as stored into the cache (app_s)
+    float kk[D / 32];
+    row_load<T, D>(app_s, kk, lane);
+    const int ha = (lane & 3) * 2;  // this lane's head columns ha, ha + 1
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) {
+      float part = 0.0f;
+      if (h < G) {
+        float qv[D / 32];
+        row_load<T, D>(q_s + h * D, qv, lane);
+#pragma unroll
+        for (int e = 0; e < D / 32; ++e) part += qv[e] * kk[e];
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(kFullMask, part, off);
+      if (h == ha) m0 = part * sl2;
+      if (h == ha + 1) m1 = part * sl2;
+    }
+    // l is kept as per-lane partial sums over the lanes of a head column (summed after
+    // the stage loop): the token counts once, in the lane with hq == 0
+    l0 = hq == 0 ? 1.0f : 0.0f;
+    l1 = hq == 0 ? 1.0f : 0.0f;
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+      const float va = to_f32<T>(app_s[D + j * 16 + hq]), vb = to_f32<T>(app_s[D + j * 16 + hq + 8]);
+      acc[j][0] = va;
+      acc[j][1] = va;
+      acc[j][2] = vb;
+      acc[j][3] = vb;
+    }
+  }
 
 #pragma unroll 1
   for (int k = 0; live > 0; k = (k + 1 == kSlots) ? 0 : k + 1) {
@@ -466,6 +507,22 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     uint8_t* sk = ring + slot * Sh::kStageBytes;
     const uint32_t bk = smem_u32(sk);
     const uint32_t bv = bk + Sh::kKBytes;
+    if (app_patch && i == append_stage && flags_s[2] != 0) {
+      // the appended token's k and v rows: 16-byte units u of row tl in chunk c at the
+      // 128-byte-swizzled position u ^ (tl % 8), as TMA lays them out
+      const int tl = (S - 1) - t0;
+      constexpr int UR = D / 8;  // 16-byte units per row
+      for (int u = lane; u < 2 * UR; u += 32) {
+        const int kind = u / UR, g = u - kind * UR;
+        const int c = g >> 3, w16 = g & 7;
+        uint8_t* dst = sk + kind * Sh::kKBytes + (tl >> lbh) * box_bytes + c * (bh * 128) + (tl & (bh - 1)) * 128 +
+                       ((w16 ^ (tl & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(app_s + kind * D + g * 8);
+      }
+      // these generic writes precede a later TMA write into the same slot
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
     if (nvalid < TOK) {
       // rows past the sequence end hold stale or unloaded data: zero V there so
       // P = 0 rows cannot turn into NaN in the PV product
@@ -672,7 +729,10 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       write_out<T>(ob, gb, qoff + idx, gidx(idx), o);
     }
   };
-  if (!aborted) {
+  const int C = p.cluster;
+  // the sum over the four warps: into the output (one split), into `mine` (a cluster
+  // of one CTA), or, in a cluster, on the way into the st.async stores below
+  if (!aborted && (nsplit == 1 || C == 1)) {
 #pragma unroll 2
     for (int idx = ctid; idx < GD; idx += kConsumerWarps * 32) {
       const int h = idx / D, d = idx - h * D;
@@ -698,7 +758,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   // its mbarrier has counted all C contributions: no cluster-wide barrier, and no CTA
   // waits at exit for its peers (its shared memory is only written, never read, by
   // them, and every write to it has landed before it merges) ----
-  const int C = p.cluster;
   const int rank = split % C;
   const int cid = split / C;
   const int nclust = nsplit / C;
@@ -707,22 +766,34 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const int hi = min(GD, lo + slice);
   const int Gp = (G + 3) & ~3;
   const int rxs = slice + Gp;  // floats of one contribution in the receive buffer
-  consumer_sync();  // this CTA's partial is complete in `mine`
+  if (C == 1) consumer_sync();  // `mine` is complete (the merge below reads it across threads)
   if (C > 1) {
     // every CTA of the cluster runs and has initialised its receive mbarrier (the
     // phase completed long ago; this orders nothing inside the CTA)
     asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
     if (slice % 4 == 0) {
-      // 16-byte stores (mine, the slices and the receive rows are 16-byte aligned);
-      // the log-sum-exp quads are padded with -inf
+      // 16-byte stores (the combine rows, the slices and the receive rows are 16-byte
+      // aligned), each the four warps' sum of four outputs of one head; the
+      // log-sum-exp quads are padded with -inf
       const int q4 = rxs / 4;
 #pragma unroll 1
       for (int i = ctid; i < C * q4; i += kConsumerWarps * 32) {
         const int c = i / q4, e = (i - c * q4) * 4;
-        float4 v;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (e < slice) {
-          if (c * slice + e >= GD) continue;
-          v = aborted ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(mine + c * slice + e);
+          const int idx = c * slice + e;
+          if (idx >= GD) continue;
+          if (!aborted) {
+            const int h = idx / D, d = idx - h * D;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+              const float4 x = *reinterpret_cast<const float4*>(co + (w * 8 + h) * kCoRow + d);
+              v.x += x.x;
+              v.y += x.y;
+              v.z += x.z;
+              v.w += x.w;
+            }
+          }
         } else {
           const int h = e - slice;
           v.x = (!aborted && h < G) ? mine[GD + h] : -INFINITY;
@@ -738,8 +809,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
         const int c = i / (slice + G), e = i - c * (slice + G);
         float v;
         if (e < slice) {
-          if (c * slice + e >= GD) continue;
-          v = aborted ? 0.0f : mine[c * slice + e];
+          const int idx = c * slice + e;
+          if (idx >= GD) continue;
+          v = 0.0f;
+          if (!aborted) {
+            const int h = idx / D, d = idx - h * D;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) v += co[(w * 8 + h) * kCoRow + d];
+          }
         } else {
           v = aborted ? -INFINITY : mine[GD + e - slice];  // an aborted CTA contributes nothing
         }
@@ -778,39 +855,55 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
   };
   float* gslot = p.part + static_cast<size_t>(part_base + cid) * pf;  // [o: G*D][lse: G]
+  // tp lanes (a power of two, as many as the slice leaves threads for) share each
+  // output: lane `sub` folds contributions sub, sub + tp, ..., and the lanes' (max,
+  // sum, weighted o) are combined by shuffles, so the serial chain is about C / tp
+  // contributions long instead of C
+  const int nout = max(0, hi - lo);
+  int tp = 1;
+  while (tp < C && tp < 32 && 2 * tp * nout <= kConsumerWarps * 32) tp *= 2;
 #pragma unroll 1
-  for (int idx = lo + ctid; idx < hi; idx += kConsumerWarps * 32) {
+  for (int t0 = 0; t0 < nout * tp; t0 += kConsumerWarps * 32) {
+    const int t = t0 + ctid;
+    const bool valid = t < nout * tp;
+    const int idx = lo + (valid ? t / tp : 0);
+    const int sub = t & (tp - 1);
     const int h = idx / D;
-    float lse_c[kMaxCluster], o_c[kMaxCluster];
-#pragma unroll
-    for (int c = 0; c < kMaxCluster; ++c) {
-      if (c < C) {
-        lse_c[c] = rx_l[c * rxs + h];
-        o_c[c] = rx_o[c * rxs + idx - o_off];
+    float mx = -INFINITY, sum = 0.0f, o = 0.0f;
+    if (valid) {
+#pragma unroll 4
+      for (int c = sub; c < C; c += tp) mx = fmaxf(mx, rx_l[c * rxs + h]);
+      if (mx != -INFINITY) {
+#pragma unroll 4
+        for (int c = sub; c < C; c += tp) {
+          const float w = exp2f(rx_l[c * rxs + h] - mx);
+          sum += w;
+          o += w * rx_o[c * rxs + idx - o_off];
+        }
       }
     }
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < kMaxCluster; ++c)
-      if (c < C) mx = fmaxf(mx, lse_c[c]);
-    const float mxu = (mx == -INFINITY) ? 0.0f : mx;
-    float sum = 0.0f, o = 0.0f;
-#pragma unroll
-    for (int c = 0; c < kMaxCluster; ++c) {
-      if (c < C) {
-        const float w = exp2f(lse_c[c] - mxu);
-        sum += w;
-        o += w * o_c[c];
-      }
+    // every lane of the warp takes part (groups of tp lanes never straddle a warp)
+    for (int off = 1; off < tp; off <<= 1) {
+      const float mx2 = __shfl_xor_sync(kFullMask, mx, off);
+      const float s2 = __shfl_xor_sync(kFullMask, sum, off);
+      const float o2 = __shfl_xor_sync(kFullMask, o, off);
+      const float M = fmaxf(mx, mx2);
+      const float a = (mx == -INFINITY) ? 0.0f : exp2f(mx - M);
+      const float b2 = (mx2 == -INFINITY) ? 0.0f : exp2f(mx2 - M);
+      sum = sum * a + s2 * b2;
+      o = o * a + o2 * b2;
+      mx = M;
     }
+    if (!valid || sub != 0) continue;
+    const float lse = sum > 0.0f ? mx + log2f(sum) : -INFINITY;
     o = sum > 0.0f ? o / sum : 0.0f;
     if (cp && nclust == 1) {
-      cp_push(idx, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY);
+      cp_push(idx, o, lse);
     } else if (nclust == 1) {
-      emit(idx, h, o, sum > 0.0f ? mxu + log2f(sum) : -INFINITY, idx == lo || idx - h * D == 0);
+      emit(idx, h, o, lse, idx == lo || idx - h * D == 0);
     } else {
       gslot[idx] = o;
-      if (idx == lo || idx - h * D == 0) gslot[GD + h] = sum > 0.0f ? mxu + log2f(sum) : -INFINITY;
+      if (idx == lo || idx - h * D == 0) gslot[GD + h] = lse;
     }
   }
   if (nclust > 1) {

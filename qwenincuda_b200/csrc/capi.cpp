@@ -336,6 +336,14 @@ extern "C" {
 
 namespace {
 
+// Stages a single-sequence call copies through the attention kernel's ring: with a fused
+// append whose token is alone in the last stage (S - 1 a multiple of the stage size),
+// that token's contribution comes from registers and its stage is not copied.
+int copied_stages(int S, int tok, uint32_t flags) {
+  const int n = (S + tok - 1) / tok;
+  return n - (((flags & QIC_FUSE_APPEND) && S > 1 && (S - 1) % tok == 0) ? 1 : 0);
+}
+
 // Splits per kv head and CTAs per cluster of a single-sequence launch over n_stages
 // pipeline stages: the caller's choice, else one wave of resident 8-CTA clusters
 // (five sixths of it with QIC_PDL), fewer for shorter sequences.
@@ -366,7 +374,13 @@ int launch_shape(const qic_decode_args* a, bool cp, int n_stages, int* n_splits_
       // 8 chained layers: d=128 S=1025 10.0 -> 8.9 us, S=2049 10.5 -> 9.5, S=4097
       // 12.0 -> 11.5; d=256 S=2049 14.0 -> 12.1, S=8193 16.7 -> 15.6.
       const int per_split = D >= 256 ? 8 : (D >= 128 ? 6 : 12);
-      const int want = std::max(8, n_stages / per_split / 8 * 8);
+      int want = std::max(8, n_stages / per_split / 8 * 8);
+      // Past 8 CTAs' rings (4 stages each, 8 at d=64) a kv head takes 16 CTAs, so no CTA
+      // waits a second round trip for a fifth stage (36 chained Qwen3-8B layers, us per
+      // layer, 8 -> 16 CTAs: S=1025 7.72 -> 6.29, S=2048 7.95 -> 6.08, S=2049 8.71 -> 8.23;
+      // d=256 S=1025 9.74 -> 9.49).
+      const int ring = D == 64 ? 8 : 4;
+      if (n_stages > 8 * ring && want < 16) want = 16;
       if (want < n_splits) {
         n_splits = want;
         if (want <= qic::kMaxCluster) cluster = want;
@@ -458,7 +472,7 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   if (rc == QIC_SUCCESS) rc = encode_kv_map(&p.tm_v, a->dtype, a->v_cache, cache_tokens, kv_dim, a->head_dim, box_h);
   if (rc != QIC_SUCCESS) return rc;
 
-  const int n_stages = (S + tok - 1) / tok;
+  const int n_stages = copied_stages(S, tok, a->flags);
   int n_splits = 0, cluster = 0;
   rc = launch_shape(a, cp != nullptr, n_stages, &n_splits, &cluster);
   if (rc != QIC_SUCCESS) return rc;
@@ -528,7 +542,7 @@ int qic_decode_launch_shape(const qic_decode_args* a, int* num_splits, int* clus
   *cluster_size = 0;
   if (S == 0) return QIC_SUCCESS;  // no launch
   const int tok = qic::stage_tokens(D);
-  return launch_shape(a, false, (S + tok - 1) / tok, num_splits, cluster_size);
+  return launch_shape(a, false, copied_stages(S, tok, a->flags), num_splits, cluster_size);
 }
 
 int qic_cp_decode_attention(const qic_decode_args* a, const qic_cp_args* cp, qic_stream_t stream) {

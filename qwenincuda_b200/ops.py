@@ -167,14 +167,15 @@ def _flags(fuse_q, fuse_append, pdl, q_gate_interleaved=False):
 
 
 def decode_launch_shape(*, num_heads, num_kv_heads, head_dim, seq_len, dtype=torch.bfloat16, pdl=False,
-                        workspace=True, num_splits=0, cluster_size=0):
+                        workspace=True, num_splits=0, cluster_size=0, fuse_append=False):
     """(splits per kv head, CTAs per cluster) that qic_decode_attention uses for this
     shape. workspace: whether the call passes one (without it the splits are merged
-    on chip only, at most 16)."""
+    on chip only, at most 16). fuse_append: QIC_FUSE_APPEND (an appended token alone
+    in the last stage is not copied, so that stage does not count)."""
     a = DecodeArgs()
     a.dtype = QIC_DTYPE_BF16 if dtype == torch.bfloat16 else QIC_DTYPE_F16
     a.num_heads, a.num_kv_heads, a.head_dim, a.seq_len = num_heads, num_kv_heads, head_dim, seq_len
-    a.flags = QIC_PDL if pdl else 0
+    a.flags = (QIC_PDL if pdl else 0) | (QIC_FUSE_APPEND if fuse_append else 0)
     a.workspace = 16 if workspace else None  # only its presence is read
     a.num_splits, a.cluster_size = num_splits, cluster_size
     n, c = ctypes.c_int(0), ctypes.c_int(0)

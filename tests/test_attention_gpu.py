@@ -214,12 +214,23 @@ def _reference_step(ref, inp, layer, paged):
     return out
 
 
-@pytest.mark.parametrize("name", ["qwen3_0p6b_s1025", "qwen35_gated_s32769"])
+# (H, Hkv, d, S, gate): the appended token alone in the last stage (S - 1 a multiple of
+# 32 tokens, 16 at d=256), whose contribution comes from registers, and beside it
+_FUSED_EXTRA = {"d64_s65": (8, 2, 64, 65, False), "d64_s70": (8, 2, 64, 70, False),
+                "d128_s33": (16, 8, 128, 33, False), "d128_s2049": (32, 8, 128, 2049, False),
+                "d256_s17": (16, 4, 256, 17, True), "d256_s18": (16, 4, 256, 18, True)}
+
+
+@pytest.mark.parametrize("name", ["qwen3_0p6b_s1025", "qwen35_gated_s32769", "qwen3_8b_s8192", *_FUSED_EXTRA])
 @pytest.mark.parametrize("paged", [True, False])
 def test_fused_decode_step_matches_reference_chain(name, paged):
-    from qwenincuda_b200.workloads import CONFIGS, make_attention_inputs
+    from qwenincuda_b200.workloads import CONFIGS, AttnConfig, make_attention_inputs
 
-    cfg = CONFIGS[name]
+    if name in _FUSED_EXTRA:
+        H, Hkv, d, S, gate = _FUSED_EXTRA[name]
+        cfg = AttnConfig(name, H, Hkv, d, S, gate=gate, seed=S)
+    else:
+        cfg = CONFIGS[name]
     dtype = torch.bfloat16
     mine = make_attention_inputs(cfg, paged=paged, layers=1, dtype=dtype)
     theirs = make_attention_inputs(cfg, paged=paged, layers=1, dtype=dtype)

@@ -101,7 +101,7 @@ def test_plan_rejects_bad_arguments():
 # holding three 128-thread CTAs per SM on 148 SMs (the host fallback when no device
 # answers the occupancy query; a B200 reports the same: grid (40, 8) at S=8192)
 SHAPES = {
-    (128, 32, 8, 1025, True): (8, 8), (128, 32, 8, 2049, True): (8, 8), (128, 32, 8, 3073, True): (16, 16),
+    (128, 32, 8, 1025, True): (16, 16), (128, 32, 8, 2049, True): (16, 16), (128, 32, 8, 3073, True): (16, 16),
     (128, 32, 8, 4097, True): (16, 16), (128, 32, 8, 6145, True): (32, 8), (128, 32, 8, 8192, True): (40, 8),
     (128, 32, 8, 8192, False): (40, 8), (128, 32, 8, 131073, True): (40, 8), (128, 32, 8, 131073, False): (48, 8),
     (256, 16, 4, 2049, True): (16, 16), (256, 16, 4, 8193, True): (64, 8), (256, 16, 4, 32769, True): (88, 8),
@@ -114,8 +114,9 @@ SHAPES = {
 @pytest.mark.parametrize("key", list(SHAPES), ids=lambda k: "d{}_h{}_kv{}_s{}_{}".format(*k))
 def test_decode_launch_shape(key):
     """qic_decode_launch_shape: one wave of resident 8-CTA clusters (five sixths with
-    QIC_PDL), about 6 (d=128) or 8 (d=256) stages per CTA below that, one cluster per
-    kv head up to 16 CTAs; never more splits than stages."""
+    QIC_PDL), about 6 (d=128) or 8 (d=256) stages per CTA below that but 16 CTAs once
+    the stages exceed 8 CTAs' rings, one cluster per kv head up to 16 CTAs; never more
+    splits than stages."""
     import torch
 
     import qwenincuda_b200 as q
@@ -126,6 +127,23 @@ def test_decode_launch_shape(key):
     assert 1 <= c <= 16 and n % c == 0 and n <= max(1, (S + tok - 1) // tok)
     if not torch.cuda.is_available():
         assert (n, c) == SHAPES[key]
+
+
+def test_decode_launch_shape_fused_append_tail():
+    """With a fused append whose token is alone in the last stage (S - 1 a multiple of
+    the stage size) that stage is not copied: S=1025 at d=128 is 32 stages, which 8 CTAs'
+    rings hold; S=1024 keeps all 32 stages either way."""
+    import torch
+
+    import qwenincuda_b200 as q
+
+    shape = lambda **kw: q.ops.decode_launch_shape(num_heads=32, num_kv_heads=8, head_dim=128, pdl=True, **kw)
+    if not torch.cuda.is_available():
+        assert shape(seq_len=1025, fuse_append=True) == (8, 8)
+        assert shape(seq_len=1025) == (16, 16)
+        assert shape(seq_len=1024, fuse_append=True) == shape(seq_len=1024) == (8, 8)
+        assert shape(seq_len=2049, fuse_append=True) == (16, 16)
+    assert shape(seq_len=2, fuse_append=True) == (1, 1)
 
 
 def test_decode_launch_shape_explicit_and_without_workspace():
