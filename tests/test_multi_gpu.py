@@ -4,8 +4,9 @@ Each rank is a spawned process on its own GPU. All ranks build the same seeded
 sequence, keep their own shard (shard_tokens) in their own shuffled page pool, map
 each other's exchange buffers with CUDA IPC (handles exchanged over a gloo process
 group) and call qic_cp_decode_attention three times. Every rank checks its output
-against the whole-sequence call made on its own GPU and against the reference's own
-chain on the whole sequence (head-norm + RoPE of q and k, row copies, paged_attention
+against the whole-sequence call made on its own GPU (also over four calls chained with
+programmatic dependent launch) and against the reference's own chain on the whole
+sequence (head-norm + RoPE of q and k, row copies, paged_attention
 of src/kernels.cu built for sm_100a), both within max-abs 2e-3 / rel 1e-2, and the
 owner of the last token checks the appended rows byte for byte. Skipped with fewer
 than two GPUs.
@@ -83,6 +84,17 @@ def _rank_main(rank, world, port, S, results):
             ok, err, idx = allclose_report(out, want, 2e-3, 1e-2)
             ok_r, err_r, _ = allclose_report(out, want_ref, 2e-3, 1e-2)
             errs.append((call, st, ok and ok_r, max(err, err_r)))
+        # four more calls chained with programmatic dependent launch, not synchronised in
+        # between: each call's K/V copies start while the previous call exchanges
+        outs = [torch.full((H * D,), float("nan"), device="cuda", dtype=qv.dtype) for _ in range(4)]
+        for o in outs:
+            cpm.cp_decode_attention(group, out=o, pdl=True, **_kw(n, qv, kc, vc, tab, w, kn, vn, False, ws,
+                                                                  position=S - 1))
+        torch.cuda.synchronize()
+        st = ws.status()
+        for i, o in enumerate(outs):
+            ok, err, idx = allclose_report(o, want, 2e-3, 1e-2)
+            errs.append((3 + i, st, ok, err))
         row_ok = True
         if last:
             lp, lf = (n - 1) // P, (S - 1) // P
