@@ -26,8 +26,10 @@
 //    accumulates in registers.
 //  * Fused options: the q prologue (head RMSNorm + RoPE of q, read from q or from
 //    the interleaved q/gate projection), the K/V append of the new token (head
-//    RMSNorm + RoPE of k written into its page slot before the stage holding it is
-//    copied), and the sigmoid output gate.
+//    RMSNorm + RoPE of k written into its page slot; a stage holding it that was
+//    copied before the append gets the row written into shared memory, and a token
+//    alone in the last stage is taken from registers without copying that stage),
+//    and the sigmoid output gate.
 //  * The splits of a kv head form thread-block clusters. CTA c of a cluster owns
 //    output slice c: every CTA sends slice c of its (o, lse) partial into CTA c's
 //    shared memory with st.async (distributed shared memory, bytes counted by CTA c's
