@@ -130,6 +130,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gated_delta_kernel(const qic_g
     prefetch_l2(conv_state + static_cast<size_t>(ck) * K);
     if (tid < NC) prefetch_l2(conv_state + static_cast<size_t>(cv) * K);
   }
+  // The step's inputs may still be written by the preceding kernel: they are only
+  // brought into L2 here (no value is read; L2 is the point of coherence, so a later
+  // write lands there) and read after the wait. One prefetch per 64-byte run of a warp.
+  if ((tid & 31) == 0) {
+    prefetch_l2(qkv + cq);
+    prefetch_l2(qkv + ck);
+    if (tid < NC) {
+      prefetch_l2(qkv + cv);
+      prefetch_l2(static_cast<const T*>(a.z) + static_cast<size_t>(vh) * kGdnDv + cb * NC + tid);
+    }
+    if (tid == 0) {
+      prefetch_l2(static_cast<const T*>(a.b) + vh);
+      prefetch_l2(static_cast<const T*>(a.a) + vh);
+    }
+  }
   const T dt_raw = static_cast<const T*>(a.dt_bias)[vh];
   const T al_raw = static_cast<const T*>(a.a_log)[vh];
   T nw_raw = T();
