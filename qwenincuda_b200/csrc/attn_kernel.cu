@@ -381,7 +381,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     }
     if (my_append) {
       if (app_ok) {
-        row_rmsnorm_w<T, D>(kr, kw, hd, p.eps);
+        // the reference's ascending-order sum of squares (app_s is free until the row
+        // is staged there below)
+        row_rmsnorm_w_staged<T, D>(kr, kw, hd, p.eps, reinterpret_cast<float*>(app_s), lane);
         row_rope_apply<T, D>(kr, rc, rs, lane);
         const size_t at = static_cast<size_t>(app_slot) * static_cast<size_t>(p.Hkv) * D + static_cast<size_t>(kvh) * D;
         row_store<T, D>(static_cast<T*>(p.k_cache) + at, kr, lane);

@@ -98,6 +98,38 @@ __device__ __forceinline__ void row_rmsnorm_w(float (&v)[D / 32], const float (&
   }
 }
 
+// row_rmsnorm_w with the same ascending-order sum computed by lane 0 from the squares
+// staged in shared memory (`scratch`: D floats, 16-byte aligned, free for this warp):
+// the same bits, without the 32*E shuffles feeding the chain.
+template <typename T, int D>
+__device__ __forceinline__ void row_rmsnorm_w_staged(float (&v)[D / 32], const float (&wv)[D / 32], int head_dim,
+                                                     float eps, float* scratch, int lane) {
+  constexpr int E = D / 32;
+#pragma unroll
+  for (int e = 0; e < E; ++e) scratch[lane * E + e] = __fmul_rn(v[e], v[e]);
+  __syncwarp();
+  float ssum = 0.0f;
+  if (lane == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(scratch);
+#pragma unroll 8
+    for (int q = 0; q < D / 4; ++q) {
+      const float4 t = s4[q];
+      ssum = __fadd_rn(ssum, t.x);
+      ssum = __fadd_rn(ssum, t.y);
+      ssum = __fadd_rn(ssum, t.z);
+      ssum = __fadd_rn(ssum, t.w);
+    }
+  }
+  ssum = __shfl_sync(kFullMask, ssum, 0);
+  __syncwarp();  // scratch may be reused after this
+  float inv_rms = rsqrtf(ssum / static_cast<float>(head_dim) + eps);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    float xv = v[e];
+    v[e] = to_f32<T>(from_f32<T>(xv * inv_rms * wv[e]));
+  }
+}
+
 // row_rmsnorm_w with the sum of squares reduced as a butterfly (5 shuffle steps instead
 // of the 32*E-step ordered chain): for rows whose bytes only feed tolerance-checked
 // results (q), not rows stored for byte comparison (the appended k).
