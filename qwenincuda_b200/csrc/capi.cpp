@@ -803,18 +803,20 @@ int gemv_rows_per_split(int K, int splits) { return ((K + splits - 1) / splits +
 
 // Split count: the caller's, else the largest cluster size from {16, 12, 8, 6, 5, 4, 3,
 // 2, 1} (at least 64 rows per CTA, rows fitting shared memory) that keeps the grid at
-// most 5/3 CTAs per SM with every tile's cluster resident at once. Swept on the
+// most 2 CTAs per SM with every tile's cluster resident at once. Swept on the
 // Qwen3-8B projections (8 chained launches each, GB/s): q/k/v 24 tiles, splits 8 /
 // 10 / 12 -> 4619 / 4361 / 3638; o 16 tiles, 12 / 13 / 16 -> 4000 / 3862 / 3023;
 // gate/up 48 tiles, 5 / 6 -> 6152 / 4528; down 16 tiles, 12 / 13 -> 5446 / 4693. More
 // CTAs (odd cluster sizes, or 2 per SM everywhere) left some clusters to a second
-// wave behind the preceding launch's CTAs.
+// wave behind the preceding launch's CTAs. The cap of 2 CTAs per SM (5/3 before)
+// changes only smaller projections (Qwen3.5-4B widths): the whole decode step, A/B on
+// one box, 521-523 -> 525-526 tokens/s.
 int gemv_splits(const qic_gemv_args* a, int n_tiles) {
   const int K = a->in_dim;
   const int min_c = (K + qic::kGemvMaxRowsPerSplit - 1) / qic::kGemvMaxRowsPerSplit;
   if (a->splits > 0) return std::max(a->splits, min_c);
   static const int kSizes[] = {16, 12, 8, 6, 5, 4, 3, 2, 1};
-  const long long cap = std::max<long long>(n_tiles, static_cast<long long>(sm_count()) * 5 / 3);
+  const long long cap = std::max<long long>(n_tiles, static_cast<long long>(sm_count()) * 2);
   for (int c : kSizes) {
     if (c < min_c) break;
     if (c > 1 && K < 64 * c) continue;
