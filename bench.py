@@ -1151,6 +1151,13 @@ def main():
         return
 
     peaks = load_peaks()
+    if args.workload == "qwen35_4b_decode_step" and args.no_extra and world == 1:
+        # profiling runs of the decode-step runner alone: one line of its figures
+        w3 = decode_step_workload()
+        r = measure_decode_step(w3, max(10, args.steps // 4), args.warmup, peaks)
+        w3["model"].close()
+        print(json.dumps({"workload": args.workload, **r}), flush=True)
+        return
     extra = {}
     partitioned_mode = world > 1 and args.workload in ("qwen3_8b_s131073", "qwen3_8b_batch64")
     if args.workload == "qwen3_8b_s131073" and world > 1:
