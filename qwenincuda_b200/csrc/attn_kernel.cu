@@ -216,6 +216,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     stage_ctr = p.stage_ctr + kvh;
   }
   const int G = p.G;
+  // The cluster merge's geometry (divisions by the runtime cluster size, done here,
+  // off the merge's path): CTA `rank` of cluster `cid` owns outputs [lo, hi).
+  const int C = p.cluster;
+  const int GD = G * D;
+  const int rank = split % C, cid = split / C, nclust = nsplit / C;
+  const int slice = (GD + C - 1) / C;
+  const int lo = rank * slice, hi = min(GD, lo + slice);
   const bool do_append = (p.flags & QIC_FUSE_APPEND) && a1 == n_copy && a1 > a0;
   const int32_t* table = p.page_table != nullptr ? p.page_table + static_cast<size_t>(b) * p.table_bstride : nullptr;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
@@ -226,9 +233,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
     if (p.cluster > 1) {
       // bytes this CTA receives in the cluster merge: from each of the C CTAs, its
       // share of this CTA's output slice and its G log-sum-exps
-      const int C = p.cluster, GD = G * D, sl = (GD + C - 1) / C, lo = (split % C) * sl;
-      const int cnt = max(0, min(GD, lo + sl) - lo);
-      const int nl = (sl % 4 == 0) ? ((G + 3) & ~3) : G;  // log-sum-exps sent (padded with 16-byte stores)
+      const int cnt = max(0, hi - lo);
+      const int nl = (slice % 4 == 0) ? ((G + 3) & ~3) : G;  // log-sum-exps sent (padded with 16-byte stores)
       mbar_init(rx_bar, 1);
       mbar_arrive_expect_tx(rx_bar, static_cast<uint32_t>(C * (cnt + nl) * 4));
     }
@@ -718,7 +724,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   auto gidx = [&](int idx) -> size_t {
     return static_cast<size_t>(kvh * G + idx / D) * qhs + (idx % D);
   };
-  const int GD = G * D;
   const int pf = partial_floats(G, D);
   constexpr bool cp = CP;
   unsigned cp_e = 0;  // exchange epoch of this call (slice mergers, context parallel)
@@ -733,7 +738,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       write_out<T>(ob, gb, qoff + idx, gidx(idx), o);
     }
   };
-  const int C = p.cluster;
   // the sum over the four warps: into the output (one split), into `mine` (a cluster
   // of one CTA), or, in a cluster, on the way into the st.async stores below
   if (!aborted && (nsplit == 1 || C == 1)) {
@@ -762,12 +766,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   // its mbarrier has counted all C contributions: no cluster-wide barrier, and no CTA
   // waits at exit for its peers (its shared memory is only written, never read, by
   // them, and every write to it has landed before it merges) ----
-  const int rank = split % C;
-  const int cid = split / C;
-  const int nclust = nsplit / C;
-  const int slice = (GD + C - 1) / C;
-  const int lo = rank * slice;
-  const int hi = min(GD, lo + slice);
   const int Gp = (G + 3) & ~3;
   const int rxs = slice + Gp;  // floats of one contribution in the receive buffer
   if (C == 1) consumer_sync();  // `mine` is complete (the merge below reads it across threads)
@@ -780,14 +778,20 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
       // aligned), each the four warps' sum of four outputs of one head; the
       // log-sum-exp quads are padded with -inf
       const int q4 = rxs / 4;
+      // item i = (destination c, quad e4): one division per thread, then steps of a
+      // CTA's thread count
+      constexpr int kStep = kConsumerWarps * 32;
+      const int step_c = kStep / q4, step_e = kStep - step_c * q4;
+      int c = ctid / q4, e4 = ctid - (ctid / q4) * q4;
 #pragma unroll 1
-      for (int i = ctid; i < C * q4; i += kConsumerWarps * 32) {
-        const int c = i / q4, e = (i - c * q4) * 4;
+      for (int i = ctid; i < C * q4; i += kStep) {
+        const int e = e4 * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool send = true;
         if (e < slice) {
           const int idx = c * slice + e;
-          if (idx >= GD) continue;
-          if (!aborted) {
+          send = idx < GD;
+          if (send && !aborted) {
             const int h = idx / D, d = idx - h * D;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) {
@@ -805,7 +809,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
           v.z = (!aborted && h + 2 < G) ? mine[GD + h + 2] : -INFINITY;
           v.w = (!aborted && h + 3 < G) ? mine[GD + h + 3] : -INFINITY;
         }
-        st_async_cluster_f32x4(rx + rank * rxs + e, rx_bar, c, v);
+        if (send) st_async_cluster_f32x4(rx + rank * rxs + e, rx_bar, c, v);
+        e4 += step_e;
+        c += step_c;
+        if (e4 >= q4) {
+          e4 -= q4;
+          ++c;
+        }
       }
     } else {
 #pragma unroll 1
