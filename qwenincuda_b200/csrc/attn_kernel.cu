@@ -269,19 +269,23 @@ __global__ void __launch_bounds__(kAttnThreads, 3) decode_attn_kernel(const __gr
   const CUtensorMap* tmap = lane < 16 ? &p.tm_k : &p.tm_v;
   const int kv_off = lane < 16 ? 0 : Sh::kKBytes;
   const int append_stage = (do_append && !tail_regs) ? n_stages_seq - 1 : -1;  // copied stage holding it
+  // token index / page size: a shift for power-of-two pages (the common case), so a
+  // refill does not wait on an integer division
+  const int lP = (P > 0 && (P & (P - 1)) == 0) ? __ffs(P) - 1 : -1;
+  auto page_of = [&](int t) -> int { return lP >= 0 ? (t >> lP) : t / P; };
   // page-table entry holding box bx of stage j, or -1
   auto box_entry = [&](int j) -> int {
     const int tb = j * TOK + bx * bh;
-    return (j >= 0 && bx * bh < TOK && tb < S) ? tb / P : -1;
+    return (j >= 0 && bx * bh < TOK && tb < S) ? page_of(tb) : -1;
   };
   auto load_entry = [&](int e) -> int { return e >= 0 ? __ldg(table + e) : 0; };
   auto issue = [&](int j, int page, int slot) {
     const int t0 = j * TOK;
-    const int nbox = (min(TOK, S - t0) + bh - 1) / bh;
+    const int nbox = (min(TOK, S - t0) + bh - 1) >> lbh;
     const int tb = t0 + bx * bh;
     long long row = tb;
     if (table != nullptr && bx < nbox) {
-      const int e = tb / P;
+      const int e = page_of(tb);
       row = static_cast<long long>(page) * P + (tb - e * P);
       if (page < 0 || (p.cache_tokens > 0 && row + bh > p.cache_tokens)) {
         record_status(p.status, QIC_DEV_BAD_PAGE);
