@@ -34,7 +34,9 @@ the full-attention layers of a hybrid stack, each with its own 32K cache),
 qwen3_8b_s131073 (single 128K sequence), qwen35_gdn (32 chained GatedDeltaNet layers,
 each with its own state; state bytes),
 qwen35_pair (GatedDeltaNet + gated attention layer), qwen3_8b_batch64 (64 sequences,
-lengths 512..32768, one shared page pool, one batched launch).
+lengths 512..32768, one shared page pool, one batched launch). Profiling runs with
+--no-extra: gemv_qwen3_8b (the projections alone) and qwen35_4b_decode_step (the
+decode-step runner alone, one line of its figures). Tuning runs: --splits, --seq-len.
 
 --impl reference (rank 0 only): the reference's implementation of the same workload
 on the host cores, as the line's value, on a bounded sample. Attention: the oracle's C
