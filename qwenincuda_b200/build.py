@@ -29,7 +29,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}
 UNITS = [
     ("attn_kernel.cu", ["--use_fast_math"]),
     ("rowops.cu", ["--use_fast_math"]),
-    ("gdn_kernel.cu", []),
+    ("gdn_kernel.cu", ["--use_fast_math"]),
     ("capi.cpp", []),
     ("compat.cu", ["--use_fast_math"]),
     ("noalloc.cu", []),
