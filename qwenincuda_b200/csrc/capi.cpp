@@ -506,7 +506,6 @@ int decode_attention_impl(const qic_decode_args* a, const qic_cp_args* cp, qic_s
   p.page_size = paged ? a->page_size : 0;
   p.box_h = box_h;
   p.log2_box_h = lbh;
-  p.n_stages = n_stages;
   p.n_splits = n_splits;
   p.seq_len_dev = dev_len ? a->seq_len_dev : nullptr;
   p.rope_pos = (a->flags & QIC_EXPLICIT_POSITION) ? a->position : -1;

@@ -90,7 +90,7 @@ struct AttnParams {
   int seq_len;
   int page_size;
   int box_h, log2_box_h;
-  int n_stages, n_splits;            // n_splits = cluster * n_clusters CTAs per kv head
+  int n_splits;                      // cluster * n_clusters CTAs per kv head (stages: from seq_len)
   int cluster;                       // CTAs per thread-block cluster along the splits
   int flags;
   float eps, theta, scale_log2;
