@@ -97,6 +97,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C = p.splits;
   const int crank = blockIdx.x;  // rank in the cluster = split of the rows
+  // the tile columns this CTA finishes after the cluster's reduction (a division by
+  // the runtime cluster size, done here rather than after the stream)
+  const int slice = (kTile + C - 1) / C;
+  const int lo = crank * slice, hi = min(kTile, lo + slice);
   const int tile = blockIdx.y;
   // the tile's segment and first column
   int s = 0;
@@ -254,8 +258,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
   }
 
   // ---- the cluster's CTAs each finish one slice of the tile's columns ----
-  const int slice = (kTile + C - 1) / C;
-  const int lo = crank * slice, hi = min(kTile, lo + slice);
   if (C > 1) {
     __syncwarp();
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
